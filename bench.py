@@ -1,0 +1,439 @@
+#!/usr/bin/env python
+"""MoC forward+backward throughput on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = the MoC module's training step on one batch of synthetic input: router
+(z @ router^T, softmax) -> convolution -> backward of both (dx, dz, dconv_bases,
+drouter).  Config 2: B=4, T=4096, D=z_dim=2048, K=16, S=4, bf16, softmax router,
+init_std 0.002, router weight N(0, 0.02); x, z, dy ~ N(0, 1) from a seeded generator.
+
+* ``value``      tokens/s of the whole job: the step is captured once in a CUDA graph
+                 and replayed K times with inputs resident in HBM (192 MiB of x, z, dy
+                 per rank, larger than the 126 MB L2), timed with CUDA events.
+* ``e2e``        the same metric through the public API (``MoC`` forward + backward,
+                 eager), with x, z, dy copied from pinned host memory every step and
+                 y, dx, dz, dconv_bases, drouter copied back inside the timed region.
+* ``roofline``   the dominant kernel timed alone (CUDA events on its stream):
+                 algorithmic bytes per launch / average launch time vs measured HBM peak.
+* ``cpu_baseline`` the CPU oracle (a port of the reference's PyTorch path) on a bounded
+                 sample, rank 0 at N=1 only.
+
+With N > 1 (torchrun, one rank per GPU) every rank runs its own config-2 batch
+(weak scaling) and the step adds one NCCL all-reduce of [dconv_bases | drouter].
+``--impl reference`` times the reference's CPU path (the oracle port) instead.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mixture-of-convolutions_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+CONFIG = {"B": 4, "T": 4096, "D": 2048, "Dz": 2048, "K": 16, "S": 4, "router": "softmax", "activation": None,
+          "init_std": 0.002, "router_std": 0.02}
+METRIC = "MoC fwd+bwd tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def step_bytes_per_token(D: int, Dz: int, K: int) -> int:
+    """Algorithmic HBM bytes per token of one module fwd+bwd (bf16): forward reads x, z
+    and writes y; backward reads dy, x, z and writes dx, dz; alpha is written once and
+    read once: 2*(5D + 3Dz) + 4K."""
+    return 2 * (5 * D + 3 * Dz) + 4 * K
+
+
+KERNEL_BYTES_PER_TOKEN = {
+    # per-launch algorithmic bytes per token (bf16): reads + writes the kernel must do
+    "conv_backward": lambda c: 2 * c["D"] * 3 + 2 * c["K"] * 2,   # x, dy in; dx out; alpha in, dalpha out
+    "conv_forward": lambda c: 2 * c["D"] * 2 + 2 * c["K"],        # x in, y out, alpha in
+    "router_forward": lambda c: 2 * c["Dz"] + 2 * c["K"],         # z in, alpha out
+    "router_backward": lambda c: 2 * c["Dz"] * 2 + 4 * c["K"],    # z in, dz out, alpha + dalpha in
+}
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "source": "fallback"}
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML every ~20 ms in a thread."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device: torch.device) -> None:
+        self.samples: list[tuple[float, int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            props = torch.cuda.get_device_properties(device)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001
+            self._nvml = None
+
+    def _run(self) -> None:
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((time.perf_counter(), mhz, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.02)
+
+    def start(self) -> None:
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self, t0: float, t1: float) -> dict:
+        if self._nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        inside = [s for s in self.samples if t0 <= s[0] <= t1] or self.samples[-3:]
+        mhz = [s[1] for s in inside]
+        mask = 0
+        for s in inside:
+            mask |= s[2]
+        reasons = [name for name, bit in self.REASONS.items() if mask & bit and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(inside)}
+
+
+# ----------------------------------------------------------------------------- workload
+
+def make_module_and_inputs(cfg: dict, rank: int, device: torch.device):
+    from moc import MoC
+
+    torch.manual_seed(1234 + rank)
+    m = MoC(dim=cfg["D"], z_dim=cfg["Dz"], kernel_size=cfg["S"], k=cfg["K"], activation=cfg["activation"],
+            init_std=cfg["init_std"], router_activation=cfg["router"])
+    g = torch.Generator().manual_seed(4321 + rank)
+    with torch.no_grad():
+        m.router.copy_(torch.randn(cfg["K"], cfg["Dz"], generator=g) * cfg["router_std"])
+    m = m.to(device=device, dtype=torch.bfloat16)
+    shape = (cfg["B"], cfg["T"])
+    host = {
+        "x": torch.randn(*shape, cfg["D"], generator=g).bfloat16(),
+        "z": torch.randn(*shape, cfg["Dz"], generator=g).bfloat16(),
+        "dy": torch.randn(*shape, cfg["D"], generator=g).bfloat16(),
+    }
+    return m, host
+
+
+def train_step(m, x, z, dy):
+    y, _ = m(x, z)
+    grads = torch.autograd.grad(y, (x, z, m.conv_bases, m.router), dy)
+    return y, grads
+
+
+def allreduce_grads(grads, flat: torch.Tensor) -> None:
+    """Sum [dconv_bases | drouter] over ranks in one fp32 NCCL all-reduce."""
+    dbasis, drouter = grads[2], grads[3]
+    n0 = dbasis.numel()
+    flat[:n0].copy_(dbasis.reshape(-1))
+    flat[n0:].copy_(drouter.reshape(-1))
+    dist.all_reduce(flat)
+
+
+def time_region(fn, steps: int, stream: torch.cuda.Stream) -> float:
+    """ms per call of fn over `steps` calls, CUDA events on `stream`."""
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+
+def cpu_baseline(cfg: dict, iters: int = 2, seq_tokens: int = 2048) -> dict:
+    """The CPU oracle (a port of the reference's moc/reference.py + router, fp32) on one
+    sequence of `seq_tokens` tokens of the config, all host threads."""
+    from oracle import moc_oracle as O
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(1, seq_tokens, cfg["D"], generator=g)
+    z = torch.randn(1, seq_tokens, cfg["Dz"], generator=g)
+    dy = torch.randn(1, seq_tokens, cfg["D"], generator=g)
+    w = torch.randn(cfg["K"], cfg["Dz"], generator=g) * cfg["router_std"]
+    b = (torch.rand(cfg["K"], cfg["S"], cfg["D"], generator=g) * 2 - 1) * cfg["init_std"] * 3 ** 0.5
+    O.module_grads(x, z, w, b, dy, cfg["router"], cfg["activation"], dtype=torch.float32)  # warm-up
+    times = []
+    for _ in range(iters):
+        t0 = time.perf_counter()
+        O.module_grads(x, z, w, b, dy, cfg["router"], cfg["activation"], dtype=torch.float32)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": seq_tokens / t, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"1 x {seq_tokens} tokens of the config, fp32 fwd+bwd, median of {iters} after 1 warm-up",
+            "sec_per_iter": t}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    cfg = dict(CONFIG)
+    seq = 2048
+    base = cpu_baseline(cfg, iters=max(1, min(args.steps, 3)), seq_tokens=seq)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["sec_per_iter"] * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2 MoC fwd+bwd (CPU sample)", "B": 1, "T": seq, "D": cfg["D"],
+                   "z_dim": cfg["Dz"], "K": cfg["K"], "S": cfg["S"], "router": cfg["router"]},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference CPU path: oracle port of moc/reference.py + router (the reference is Python; "
+                "its GPU path is Triton, not timed here)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- main
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    from moc import _lib
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
+    cfg = dict(CONFIG)
+    N_rank = cfg["B"] * cfg["T"]
+
+    m, host = make_module_and_inputs(cfg, rank, device)
+    x = host["x"].to(device).requires_grad_()
+    z = host["z"].to(device).requires_grad_()
+    dy = host["dy"].to(device)
+    n_flat = m.conv_bases.numel() + m.router.numel()
+    flat = torch.empty(n_flat, dtype=torch.float32, device=device)
+
+    # --- device-resident step, captured in a CUDA graph
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(args.warmup):
+            train_step(m, x, z, dy)
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count()
+    train_step(m, x, z, dy)
+    torch.cuda.synchronize()
+    launches_per_step = _lib.launch_count() - launches0
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        _, g_grads = train_step(m, x, z, dy)
+    stream = torch.cuda.current_stream(device)
+
+    def graph_step():
+        graph.replay()
+        if world > 1:
+            allreduce_grads(g_grads, flat)
+
+    for _ in range(args.warmup):
+        graph_step()
+    sampler = ClockSampler(device)
+    sampler.start()
+    barrier(world)
+    t_wall0 = time.perf_counter()
+    ms_step = time_region(graph_step, args.steps, stream)
+    t_wall1 = time.perf_counter()
+    barrier(world)
+    ms_step = max_over_ranks(ms_step, world)
+    clocks = sampler.summary(t_wall0, t_wall1)
+
+    # --- end to end through the public API, host buffers
+    pin = {k: v.pin_memory() for k, v in host.items()}
+    out_host = {
+        "y": torch.empty_like(pin["x"]).pin_memory(), "dx": torch.empty_like(pin["x"]).pin_memory(),
+        "dz": torch.empty_like(pin["z"]).pin_memory(),
+        "dbasis": torch.empty(m.conv_bases.shape, dtype=torch.bfloat16).pin_memory(),
+        "drouter": torch.empty(m.router.shape, dtype=torch.bfloat16).pin_memory(),
+    }
+    xd = torch.empty_like(x.detach())
+    zd = torch.empty_like(z.detach())
+    dyd = torch.empty_like(dy)
+
+    def e2e_step():
+        xd.copy_(pin["x"], non_blocking=True)
+        zd.copy_(pin["z"], non_blocking=True)
+        dyd.copy_(pin["dy"], non_blocking=True)
+        xg = xd.detach().requires_grad_()
+        zg = zd.detach().requires_grad_()
+        y, grads = train_step(m, xg, zg, dyd)
+        if world > 1:
+            allreduce_grads(grads, flat)
+        for name, t in (("y", y), ("dx", grads[0]), ("dz", grads[1]), ("dbasis", grads[2]),
+                        ("drouter", grads[3])):
+            out_host[name].copy_(t.detach(), non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    barrier(world)
+    ms_e2e = max_over_ranks(time_region(e2e_step, e2e_steps, stream), world)
+    h2d = sum(t.numel() * t.element_size() for t in pin.values())
+    d2h = sum(t.numel() * t.element_size() for t in out_host.values())
+
+    # --- per-kernel timing for the roofline (each C-ABI call timed alone)
+    import moc.ops as ops
+
+    xa = x.detach()
+    with torch.no_grad():
+        alpha = ops.launch_router_forward(z.detach(), m.router.detach(), cfg["router"])
+    basis = m.conv_bases.detach()
+    kernel_calls = {
+        "router_forward": lambda: ops.launch_router_forward(z.detach(), m.router.detach(), cfg["router"]),
+        "conv_forward": lambda: ops.launch_forward(xa, alpha, basis, activation_flag=0),
+        "conv_backward": lambda: ops.launch_backward(xa, alpha, basis, dy, dy, activation_flag=0, need_x=True),
+        "router_backward": lambda: ops.launch_router_backward(z.detach(), m.router.detach(), alpha, alpha,
+                                                              cfg["router"]),
+    }
+    kernel_ms = {}
+    reps = max(5, min(args.steps, 20))
+    for name, fn in kernel_calls.items():
+        fn()
+        kernel_ms[name] = time_region(fn, reps, stream)
+    dominant = max(kernel_ms, key=kernel_ms.get)
+    peaks = measured_peaks()
+    kbytes = KERNEL_BYTES_PER_TOKEN[dominant](cfg) * N_rank
+    achieved = kbytes / (kernel_ms[dominant] * 1e-3) / 1e9
+    traffic = profiled_traffic(dominant)
+
+    step_bytes = step_bytes_per_token(cfg["D"], cfg["Dz"], cfg["K"]) * N_rank
+    tokens_all = N_rank * world
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": tokens_all / (ms_step * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "config2: MoC module fwd+bwd, B=4 T=4096 D=z_dim=2048 K=16 S=4 bf16 softmax",
+                       "global_batch": cfg["B"] * world, "seq_len": cfg["T"], "D": cfg["D"], "z_dim": cfg["Dz"],
+                       "K": cfg["K"], "S": cfg["S"], "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (x, z, dy = 192 MiB per rank)",
+                       "timing": "CUDA graph of one step replayed K times; CUDA events; max over ranks"},
+            "achieved_gbs": step_bytes / (ms_step * 1e-3) / 1e9,
+            "step_hbm_frac": step_bytes / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"],
+            "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
+                         "peak_source": peaks["source"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                         "traffic": traffic, "launch_ms": kernel_ms[dominant],
+                         "algorithmic_bytes_per_launch": kbytes},
+            "kernel_ms": kernel_ms,
+            "e2e": {"value": tokens_all / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            base = cpu_baseline(cfg)
+            line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+
+    sampler.stop()
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def profiled_traffic(kernel: str):
+    """DRAM bytes per launch of `kernel` at this workload, from the committed ncu summary
+    (profiles/*.md line 'traffic_bytes_per_launch <kernel> <bytes>'), else None."""
+    pdir = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(pdir):
+        return None
+    for name in sorted(os.listdir(pdir)):
+        if not name.endswith(".md"):
+            continue
+        with open(os.path.join(pdir, name)) as f:
+            for line in f:
+                parts = line.strip().strip("`").split()
+                if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch" and parts[1] == kernel:
+                    return float(parts[2])
+    return None
+
+
+if __name__ == "__main__":
+    main()

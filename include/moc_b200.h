@@ -1,0 +1,159 @@
+/*
+ * moc_b200.h — C ABI of the B200 (sm_100a) Mixture-of-Convolutions kernels.
+ *
+ * Every entry point takes caller-owned device pointers, plain sizes and a
+ * cudaStream_t passed as `void*` (NULL = legacy default stream).  Nothing here
+ * allocates device memory or synchronises the host; work is stream ordered.
+ * Each call returns MOC_OK (0) or one of the MOC_ERR_* codes below;
+ * moc_error_string() turns a code into text.
+ *
+ * Tensor layouts (all row major, innermost dimension contiguous):
+ *   x, out, dy, dx          [n_tokens, dim]        (fixed length: n_tokens = batch*seq_len,
+ *                                                   token row = b*seq_len + t)
+ *   alpha, dalpha           [n_tokens, n_bases]
+ *   basis, dbasis           [n_bases, kernel_size, dim]
+ *   z, dz                   [n_tokens, z_dim]
+ *   router weight, dweight  [n_bases, z_dim]
+ *   decode cache            [batch, dim, kernel_size] with explicit strides
+ *
+ * Convolution convention (matches the reference's moc/kernels.py:99-130 and
+ * moc/reference.py:28-32): tap s multiplies token t-(S-1-s), so tap S-1 is the
+ * current token; taps that fall before the start of the token's sequence read 0.
+ */
+#ifndef MOC_B200_H
+#define MOC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* floating point storage types */
+#define MOC_DTYPE_F32 0
+#define MOC_DTYPE_F16 1
+#define MOC_DTYPE_BF16 2
+/* integer index types (cu_seqlens, chunk_indices) */
+#define MOC_INDEX_I32 0
+#define MOC_INDEX_I64 1
+
+/* return codes */
+#define MOC_OK 0
+#define MOC_ERR_INVALID_ARGUMENT 1
+#define MOC_ERR_UNSUPPORTED_DTYPE 2
+#define MOC_ERR_UNSUPPORTED_SHAPE 3
+#define MOC_ERR_MISALIGNED 4
+#define MOC_ERR_WORKSPACE_TOO_SMALL 5
+#define MOC_ERR_CUDA 6
+
+/* Shape and routing of one convolution problem.
+ * Fixed length: batch > 0, seq_len > 0, n_tokens = batch*seq_len, varlen fields zero/NULL.
+ * Packed varlen: batch = seq_len = 0; cu_seqlens has n_seqs+1 monotone offsets into the
+ * n_tokens rows; chunk_indices holds n_chunks (seq_id, chunk_in_seq) pairs, each covering
+ * chunk_size tokens of that sequence (the reference's prepare_chunk_indices format,
+ * moc/ops.py:47-104).  Only the listed chunks are computed. */
+typedef struct moc_problem {
+  int64_t batch;
+  int64_t seq_len;
+  int64_t n_tokens;
+  int64_t dim;
+  int32_t n_bases;
+  int32_t kernel_size;
+  int32_t x_dtype;     /* MOC_DTYPE_F32 or MOC_DTYPE_BF16: selects fp32 or bf16 compute */
+  int32_t alpha_dtype; /* any MOC_DTYPE_* */
+  int32_t basis_dtype; /* any MOC_DTYPE_* */
+  int32_t activation;  /* 0 = none, 1 = SiLU applied to the convolution output */
+  const void* cu_seqlens;
+  int32_t cu_seqlens_dtype;
+  int64_t n_seqs;
+  const void* chunk_indices;
+  int32_t chunk_indices_dtype;
+  int64_t n_chunks;
+  int32_t chunk_size;
+} moc_problem;
+
+/* Library identification, e.g. "moc_b200 0.1.0 sm_100a". */
+const char* moc_version(void);
+/* Static text for a MOC_* return code. */
+const char* moc_error_string(int code);
+/* Text of the last CUDA error seen by the library on this host thread (or ""). */
+const char* moc_last_cuda_error(void);
+
+/* Number of kernels this library has launched in this process (all devices, all
+ * streams); lets a caller count launches over a region of work. */
+uint64_t moc_launch_count(void);
+
+/* Kernel family selection for every later call in this process: MOC_PATH_AUTO (tensor
+ * cores for the bf16 shapes they support, the default) or MOC_PATH_GENERIC (the fp32
+ * CUDA-core kernels for every shape).  Both compute the complete result; the switch
+ * exists so the two families can be cross-checked through this ABI. */
+#define MOC_PATH_AUTO 0
+#define MOC_PATH_GENERIC 1
+int moc_set_kernel_path(int path);
+
+/* Forward convolution: out = [silu](conv(x, alpha, basis)), out has x's dtype.
+ * Replaces launch_forward / launch_preact, moc/ops.py:129-194 and 197-213
+ * (launch_preact is this call with activation = 0). */
+int moc_forward(const moc_problem* p, const void* x, const void* alpha, const void* basis,
+                void* out, void* stream);
+
+/* Bytes of scratch memory moc_backward needs for problem p. */
+size_t moc_backward_workspace_bytes(const moc_problem* p);
+
+/* Backward convolution.  dy is the gradient of out.  With activation = 1 the
+ * pre-activation is recomputed on chip.  Writes dx (x dtype; pass NULL to skip, the
+ * reference's need_x = False), dalpha (alpha dtype) and dbasis (basis dtype).
+ * dbasis is reduced deterministically (fixed-order two-pass sum, no atomics).
+ * Replaces launch_backward, moc/ops.py:216-338. */
+int moc_backward(const moc_problem* p, const void* x, const void* alpha, const void* basis,
+                 const void* dy, void* dx, void* dalpha, void* dbasis,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Single-token decode step against the conv cache.  x [batch, dim], alpha
+ * [batch, n_bases], basis [n_bases, kernel_size, dim]; cache [batch, dim, kernel_size]
+ * is addressed through cache_strides (in elements) and updated in place: slots 1..S-1
+ * shift to 0..S-2 and x is written to slot S-1.  out [batch, dim] has x's dtype.
+ * Replaces launch_update, moc/ops.py:341-362 (kernel moc/kernels.py:442-550). */
+int moc_step(int64_t batch, int64_t dim, int32_t n_bases, int32_t kernel_size,
+             int32_t x_dtype, int32_t alpha_dtype, int32_t basis_dtype, int32_t activation,
+             const void* x, const void* alpha, const void* basis,
+             void* cache, const int64_t cache_strides[3], void* out, void* stream);
+
+/* Router forward: alpha = act(z @ weight^T), act = softmax over n_bases (router_act 0)
+ * or exp (router_act 1).  z [n_tokens, z_dim], weight [n_bases, z_dim], alpha
+ * [n_tokens, n_bases]; all three share one dtype (f32, f16 or bf16); logits stay in fp32.
+ * Replaces the router in MoC.forward, moc/api.py:383-388 (F.linear + softmax/exp). */
+int moc_router_forward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t dtype,
+                       int32_t router_act, const void* z, const void* weight, void* alpha,
+                       void* stream);
+
+/* Bytes of scratch memory moc_router_backward needs. */
+size_t moc_router_backward_workspace_bytes(int64_t n_tokens, int64_t z_dim, int32_t n_bases,
+                                           int32_t dtype);
+
+/* Router backward from dalpha: dlogits = softmax/exp Jacobian applied to dalpha,
+ * dz = dlogits @ weight (pass NULL to skip), dweight = dlogits^T @ z (pass NULL to skip;
+ * reduced deterministically).  alpha is the forward output.  dalpha may have any
+ * float dtype; z, weight, alpha, dz and dweight share `dtype`.
+ * Replaces PyTorch autograd of moc/api.py:383-388. */
+int moc_router_backward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t dtype,
+                        int32_t router_act, const void* z, const void* weight,
+                        const void* alpha, const void* dalpha, int32_t dalpha_dtype,
+                        void* dz, void* dweight, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/* Device-side chunk index builder for packed varlen (no host sync): fills
+ * chunk_indices [n_chunks, 2] int32 with (seq_id, chunk_in_seq) for every
+ * chunk_size-token chunk of every sequence, in order.  n_chunks must equal
+ * sum(ceil(len_i / chunk_size)); the caller computes it (e.g. from cu_seqlens_cpu).
+ * Replaces the tensor arithmetic of prepare_chunk_indices, moc/ops.py:82-97. */
+int moc_prepare_chunk_indices(const void* cu_seqlens, int32_t cu_seqlens_dtype, int64_t n_seqs,
+                              int32_t chunk_size, int32_t* chunk_indices, int64_t n_chunks,
+                              void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOC_B200_H */

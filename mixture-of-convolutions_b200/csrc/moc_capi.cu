@@ -1,0 +1,176 @@
+// extern "C" entry points declared in include/moc_b200.h: argument checks, then
+// dispatch to the tensor-core kernels (bf16 shapes they support) or the generic
+// CUDA-core kernels.  No entry point allocates memory or synchronises the host.
+#include <atomic>
+#include <cstdlib>
+#include <string>
+
+#include "moc_common.cuh"
+#include "moc_internal.h"
+
+namespace moc {
+
+static thread_local std::string g_last_cuda_error;
+static int g_kernel_path = 0;  // 0 = auto, 1 = generic CUDA-core kernels only
+static std::atomic<uint64_t> g_launches{0};
+
+void note_launch(int n) { g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
+
+int note_cuda(cudaError_t e) {
+  if (e == cudaSuccess) return MOC_OK;
+  g_last_cuda_error = std::string(cudaGetErrorName(e)) + ": " + cudaGetErrorString(e);
+  return MOC_ERR_CUDA;
+}
+
+static bool valid_float_dtype(int d) { return d == MOC_DTYPE_F32 || d == MOC_DTYPE_F16 || d == MOC_DTYPE_BF16; }
+static bool valid_index_dtype(int d) { return d == MOC_INDEX_I32 || d == MOC_INDEX_I64; }
+
+static int check_problem(const moc_problem* p) {
+  if (p == nullptr) return MOC_ERR_INVALID_ARGUMENT;
+  if (p->x_dtype != MOC_DTYPE_F32 && p->x_dtype != MOC_DTYPE_BF16) return MOC_ERR_UNSUPPORTED_DTYPE;
+  if (!valid_float_dtype(p->alpha_dtype) || !valid_float_dtype(p->basis_dtype)) return MOC_ERR_UNSUPPORTED_DTYPE;
+  if (p->dim <= 0 || p->n_bases <= 0 || p->kernel_size <= 0 || p->n_tokens < 0) return MOC_ERR_INVALID_ARGUMENT;
+  if (p->n_bases > kMaxBasesSimt || p->kernel_size > kMaxKernelSize) return MOC_ERR_UNSUPPORTED_SHAPE;
+  if (p->activation != 0 && p->activation != 1) return MOC_ERR_INVALID_ARGUMENT;
+  if (p->cu_seqlens == nullptr) {
+    if (p->batch <= 0 || p->seq_len <= 0 || p->batch * p->seq_len != p->n_tokens) return MOC_ERR_INVALID_ARGUMENT;
+  } else {
+    if (p->n_seqs < 1 || p->chunk_size <= 0 || p->n_chunks < 0) return MOC_ERR_INVALID_ARGUMENT;
+    if (!valid_index_dtype(p->cu_seqlens_dtype) || !valid_index_dtype(p->chunk_indices_dtype))
+      return MOC_ERR_UNSUPPORTED_DTYPE;
+    if (p->n_chunks > 0 && p->chunk_indices == nullptr) return MOC_ERR_INVALID_ARGUMENT;
+  }
+  return MOC_OK;
+}
+
+static bool use_tc(const moc_problem& p) { return g_kernel_path == 0 && tc_conv_supported(p); }
+
+}  // namespace moc
+
+using namespace moc;
+
+extern "C" {
+
+const char* moc_version(void) { return "moc_b200 0.1.0 sm_100a"; }
+
+const char* moc_error_string(int code) {
+  switch (code) {
+    case MOC_OK: return "ok";
+    case MOC_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case MOC_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype";
+    case MOC_ERR_UNSUPPORTED_SHAPE: return "unsupported shape (n_bases > 128 or kernel_size > 64)";
+    case MOC_ERR_MISALIGNED: return "pointer not aligned for vector access";
+    case MOC_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case MOC_ERR_CUDA: return "CUDA error (see moc_last_cuda_error)";
+    default: return "unknown error code";
+  }
+}
+
+const char* moc_last_cuda_error(void) { return g_last_cuda_error.c_str(); }
+
+uint64_t moc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+// Selects the kernel family: 0 = automatic (tensor cores where supported),
+// 1 = generic CUDA-core kernels for every shape.  Both compute the full result.
+int moc_set_kernel_path(int path) {
+  if (path != 0 && path != 1) return MOC_ERR_INVALID_ARGUMENT;
+  g_kernel_path = path;
+  return MOC_OK;
+}
+
+int moc_forward(const moc_problem* p, const void* x, const void* alpha, const void* basis, void* out,
+                void* stream) {
+  int rc = check_problem(p);
+  if (rc != MOC_OK) return rc;
+  if (p->n_tokens == 0) return MOC_OK;
+  if (!x || !alpha || !basis || !out) return MOC_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (use_tc(*p)) return tc_forward(*p, x, alpha, basis, out, st);
+  return simt_forward(*p, x, alpha, basis, out, st);
+}
+
+size_t moc_backward_workspace_bytes(const moc_problem* p) {
+  if (check_problem(p) != MOC_OK) return 0;
+  return use_tc(*p) ? tc_backward_ws(*p) : simt_backward_ws(*p);
+}
+
+int moc_backward(const moc_problem* p, const void* x, const void* alpha, const void* basis, const void* dy,
+                 void* dx, void* dalpha, void* dbasis, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_problem(p);
+  if (rc != MOC_OK) return rc;
+  if (!basis || !dbasis) return MOC_ERR_INVALID_ARGUMENT;
+  if (p->n_tokens > 0 && (!x || !alpha || !dy || !dalpha)) return MOC_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (use_tc(*p)) {
+    if (workspace_bytes < tc_backward_ws(*p)) return MOC_ERR_WORKSPACE_TOO_SMALL;
+    return tc_backward(*p, x, alpha, basis, dy, dx, dalpha, dbasis, workspace, workspace_bytes, st);
+  }
+  if (workspace_bytes < simt_backward_ws(*p)) return MOC_ERR_WORKSPACE_TOO_SMALL;
+  return simt_backward(*p, x, alpha, basis, dy, dx, dalpha, dbasis, workspace, workspace_bytes, st);
+}
+
+int moc_step(int64_t batch, int64_t dim, int32_t n_bases, int32_t kernel_size, int32_t x_dtype,
+             int32_t alpha_dtype, int32_t basis_dtype, int32_t activation, const void* x, const void* alpha,
+             const void* basis, void* cache, const int64_t cache_strides[3], void* out, void* stream) {
+  if (x_dtype != MOC_DTYPE_F32 && x_dtype != MOC_DTYPE_BF16) return MOC_ERR_UNSUPPORTED_DTYPE;
+  if (!valid_float_dtype(alpha_dtype) || !valid_float_dtype(basis_dtype)) return MOC_ERR_UNSUPPORTED_DTYPE;
+  if (batch < 0 || dim <= 0 || n_bases <= 0 || kernel_size <= 0) return MOC_ERR_INVALID_ARGUMENT;
+  if (activation != 0 && activation != 1) return MOC_ERR_INVALID_ARGUMENT;
+  if (batch > 65535) return MOC_ERR_UNSUPPORTED_SHAPE;
+  if (batch == 0) return MOC_OK;
+  if (!x || !alpha || !basis || !cache || !cache_strides || !out) return MOC_ERR_INVALID_ARGUMENT;
+  return simt_step(batch, dim, n_bases, kernel_size, x_dtype, alpha_dtype, basis_dtype, activation, x, alpha,
+                   basis, cache, cache_strides, out, static_cast<cudaStream_t>(stream));
+}
+
+int moc_router_forward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t dtype, int32_t router_act,
+                       const void* z, const void* weight, void* alpha, void* stream) {
+  if (!valid_float_dtype(dtype)) return MOC_ERR_UNSUPPORTED_DTYPE;
+  if (n_tokens < 0 || z_dim <= 0 || n_bases <= 0 || (router_act != 0 && router_act != 1))
+    return MOC_ERR_INVALID_ARGUMENT;
+  if (n_bases > kMaxBasesSimt) return MOC_ERR_UNSUPPORTED_SHAPE;
+  if (n_tokens == 0) return MOC_OK;
+  if (!z || !weight || !alpha) return MOC_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (g_kernel_path == 0 && tc_router_supported(n_tokens, z_dim, n_bases, dtype))
+    return tc_router_forward(n_tokens, z_dim, n_bases, router_act, z, weight, alpha, st);
+  return simt_router_forward(n_tokens, z_dim, n_bases, dtype, router_act, z, weight, alpha, st);
+}
+
+size_t moc_router_backward_workspace_bytes(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t dtype) {
+  if (n_tokens < 0 || z_dim <= 0 || n_bases <= 0) return 0;
+  if (g_kernel_path == 0 && tc_router_supported(n_tokens, z_dim, n_bases, dtype))
+    return tc_router_backward_ws(n_tokens, z_dim, n_bases);
+  return simt_router_backward_ws(n_tokens, z_dim, n_bases);
+}
+
+int moc_router_backward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t dtype, int32_t router_act,
+                        const void* z, const void* weight, const void* alpha, const void* dalpha,
+                        int32_t dalpha_dtype, void* dz, void* dweight, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  if (!valid_float_dtype(dtype) || !valid_float_dtype(dalpha_dtype)) return MOC_ERR_UNSUPPORTED_DTYPE;
+  if (n_tokens < 0 || z_dim <= 0 || n_bases <= 0 || (router_act != 0 && router_act != 1))
+    return MOC_ERR_INVALID_ARGUMENT;
+  if (n_bases > kMaxBasesSimt) return MOC_ERR_UNSUPPORTED_SHAPE;
+  if (n_tokens > 0 && (!z || !weight || !alpha || !dalpha)) return MOC_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (g_kernel_path == 0 && tc_router_supported(n_tokens, z_dim, n_bases, dtype)) {
+    if (workspace_bytes < tc_router_backward_ws(n_tokens, z_dim, n_bases)) return MOC_ERR_WORKSPACE_TOO_SMALL;
+    return tc_router_backward(n_tokens, z_dim, n_bases, router_act, z, weight, alpha, dalpha, dalpha_dtype, dz,
+                              dweight, workspace, workspace_bytes, st);
+  }
+  if (workspace_bytes < simt_router_backward_ws(n_tokens, z_dim, n_bases)) return MOC_ERR_WORKSPACE_TOO_SMALL;
+  return simt_router_backward(n_tokens, z_dim, n_bases, dtype, router_act, z, weight, alpha, dalpha, dalpha_dtype,
+                              dz, dweight, workspace, workspace_bytes, st);
+}
+
+int moc_prepare_chunk_indices(const void* cu_seqlens, int32_t cu_seqlens_dtype, int64_t n_seqs, int32_t chunk_size,
+                              int32_t* chunk_indices, int64_t n_chunks, void* stream) {
+  if (!valid_index_dtype(cu_seqlens_dtype)) return MOC_ERR_UNSUPPORTED_DTYPE;
+  if (n_seqs < 0 || chunk_size <= 0 || n_chunks < 0) return MOC_ERR_INVALID_ARGUMENT;
+  if (n_chunks > 0 && (!cu_seqlens || !chunk_indices)) return MOC_ERR_INVALID_ARGUMENT;
+  return build_chunk_indices(cu_seqlens, cu_seqlens_dtype == MOC_INDEX_I64, n_seqs, chunk_size, chunk_indices,
+                             n_chunks, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

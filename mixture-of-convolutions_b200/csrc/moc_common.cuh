@@ -1,0 +1,150 @@
+// Shared device helpers for the MoC kernels: dtype conversion, the bf16 rounding
+// points of the reference's bf16 compute mode, and the token-row mapping that turns
+// a fixed-length batch or a packed varlen chunk list into row ranges.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/moc_b200.h"
+
+namespace moc {
+
+using bf16 = __nv_bfloat16;
+
+// ---------------------------------------------------------------- conversions
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(bf16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ bf16 from_f32<bf16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+// Load element `i` of a tensor whose storage type is only known at run time.
+// The branch is uniform across a warp, so it costs a predicate, not divergence.
+__device__ __forceinline__ float ld_any(const void* p, int dtype, int64_t i) {
+  if (dtype == MOC_DTYPE_BF16) return __bfloat162float(static_cast<const bf16*>(p)[i]);
+  if (dtype == MOC_DTYPE_F16) return __half2float(static_cast<const __half*>(p)[i]);
+  return static_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void st_any(void* p, int dtype, int64_t i, float v) {
+  if (dtype == MOC_DTYPE_BF16)
+    static_cast<bf16*>(p)[i] = __float2bfloat16_rn(v);
+  else if (dtype == MOC_DTYPE_F16)
+    static_cast<__half*>(p)[i] = __float2half_rn(v);
+  else
+    static_cast<float*>(p)[i] = v;
+}
+
+// In bf16 compute mode the reference rounds alpha, basis and the dz*x product to
+// bf16 before each contraction (moc/kernels.py:92-95, 125-128, 390-392); in fp32
+// mode values pass through unchanged.
+template <bool BF16>
+__device__ __forceinline__ float cround(float v) {
+  if constexpr (BF16) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+  } else {
+    return v;
+  }
+}
+
+__device__ __forceinline__ int64_t ld_index(const void* p, int is_i64, int64_t i) {
+  return is_i64 ? static_cast<const int64_t*>(p)[i] : static_cast<int64_t>(static_cast<const int32_t*>(p)[i]);
+}
+
+// SiLU and its derivative, in the reference's form (moc/kernels.py:132-133, 231-232).
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+__device__ __forceinline__ float dsilu_f(float v) {
+  const float sig = 1.0f / (1.0f + expf(-v));
+  return sig * (1.0f + v * (1.0f - sig));
+}
+
+// ------------------------------------------------------------------ row mapping
+
+// A work item is a run of consecutive token rows [r0, r1) inside one sequence whose
+// rows are [seq_start, seq_end).  Fixed length: item i is tile (i % tiles) of sequence
+// (i / tiles).  Varlen: item i is chunk_indices[i] = (seq_id, chunk) of chunk_size rows,
+// the reference's packed-chunk scheme (moc/kernels.py:57-76).  Items whose indices point
+// outside the problem are reported empty rather than read out of bounds.
+struct RowMap {
+  int64_t batch = 0, seq_len = 0, n_tokens = 0;
+  int64_t tiles_per_seq = 0;
+  int32_t tile = 0;
+  int32_t varlen = 0;
+  const void* cu = nullptr;
+  int32_t cu_i64 = 0;
+  int64_t n_seqs = 0;
+  const void* chunks = nullptr;
+  int32_t ch_i64 = 0;
+  int64_t n_chunks = 0;
+  int32_t chunk_size = 0;
+
+  __host__ __device__ int64_t n_items() const { return varlen ? n_chunks : batch * tiles_per_seq; }
+  // Rows per item (upper bound).
+  __host__ __device__ int32_t item_rows() const { return varlen ? chunk_size : tile; }
+
+  __device__ __forceinline__ bool item(int64_t i, int64_t& seq_start, int64_t& seq_end, int64_t& r0,
+                                       int64_t& r1) const {
+    if (!varlen) {
+      const int64_t b = i / tiles_per_seq;
+      const int64_t c = i - b * tiles_per_seq;
+      seq_start = b * seq_len;
+      seq_end = seq_start + seq_len;
+      r0 = seq_start + c * tile;
+      r1 = r0 + tile < seq_end ? r0 + tile : seq_end;
+      return r0 < r1;
+    }
+    const int64_t sid = ld_index(chunks, ch_i64, 2 * i);
+    const int64_t c = ld_index(chunks, ch_i64, 2 * i + 1);
+    if (sid < 0 || sid >= n_seqs || c < 0) return false;
+    seq_start = ld_index(cu, cu_i64, sid);
+    seq_end = ld_index(cu, cu_i64, sid + 1);
+    if (seq_start < 0 || seq_end > n_tokens || seq_end <= seq_start) return false;
+    if (c > (seq_end - seq_start) / chunk_size) return false;
+    r0 = seq_start + c * chunk_size;
+    r1 = r0 + chunk_size < seq_end ? r0 + chunk_size : seq_end;
+    return r0 < r1;
+  }
+};
+
+inline RowMap make_rowmap(const moc_problem& p, int32_t fixed_tile) {
+  RowMap m;
+  m.n_tokens = p.n_tokens;
+  if (p.cu_seqlens != nullptr) {
+    m.varlen = 1;
+    m.cu = p.cu_seqlens;
+    m.cu_i64 = p.cu_seqlens_dtype == MOC_INDEX_I64;
+    m.n_seqs = p.n_seqs;
+    m.chunks = p.chunk_indices;
+    m.ch_i64 = p.chunk_indices_dtype == MOC_INDEX_I64;
+    m.n_chunks = p.n_chunks;
+    m.chunk_size = p.chunk_size;
+  } else {
+    m.batch = p.batch;
+    m.seq_len = p.seq_len;
+    m.tile = fixed_tile;
+    m.tiles_per_seq = (p.seq_len + fixed_tile - 1) / fixed_tile;
+  }
+  return m;
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Counts kernel launches for moc_launch_count(); call once per <<<>>> launch.
+void note_launch(int n = 1);
+
+// Records the last CUDA error for moc_last_cuda_error(); returns MOC_ERR_CUDA or MOC_OK.
+int note_cuda(cudaError_t e);
+
+}  // namespace moc

@@ -1,0 +1,52 @@
+// Internal launcher interface between the C ABI (moc_capi.cu) and the kernel files.
+// Launchers validate nothing the C ABI already checked; they return MOC_* codes.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/moc_b200.h"
+
+namespace moc {
+
+// ---- generic CUDA-core path: any dtype mix, any K <= 128, any S <= 64 (moc_simt.cu)
+int simt_forward(const moc_problem& p, const void* x, const void* alpha, const void* basis, void* out,
+                 cudaStream_t st);
+size_t simt_backward_ws(const moc_problem& p);
+int simt_backward(const moc_problem& p, const void* x, const void* alpha, const void* basis, const void* dy,
+                  void* dx, void* dalpha, void* dbasis, void* ws, size_t ws_bytes, cudaStream_t st);
+int simt_step(int64_t B, int64_t D, int K, int S, int x_dtype, int a_dtype, int b_dtype, int act, const void* x,
+              const void* alpha, const void* basis, void* cache, const int64_t cs[3], void* out,
+              cudaStream_t st);
+int simt_router_forward(int64_t N, int64_t Dz, int K, int dtype, int act, const void* z, const void* w,
+                        void* alpha, cudaStream_t st);
+size_t simt_router_backward_ws(int64_t N, int64_t Dz, int K);
+int simt_router_backward(int64_t N, int64_t Dz, int K, int dtype, int act, const void* z, const void* w,
+                         const void* alpha, const void* dalpha, int da_dtype, void* dz, void* dw, void* ws,
+                         size_t ws_bytes, cudaStream_t st);
+int build_chunk_indices(const void* cu, int cu_i64, int64_t n_seqs, int chunk, int32_t* out, int64_t n_chunks,
+                        cudaStream_t st);
+
+// ---- tensor-core path for bf16 x/alpha/basis (moc_tc.cu); *_supported says whether
+// the problem fits its templates, otherwise the caller uses the generic path.
+bool tc_conv_supported(const moc_problem& p);
+int tc_forward(const moc_problem& p, const void* x, const void* alpha, const void* basis, void* out,
+               cudaStream_t st);
+size_t tc_backward_ws(const moc_problem& p);
+int tc_backward(const moc_problem& p, const void* x, const void* alpha, const void* basis, const void* dy,
+                void* dx, void* dalpha, void* dbasis, void* ws, size_t ws_bytes, cudaStream_t st);
+
+// ---- tensor-core router for bf16 (moc_router_tc.cu)
+bool tc_router_supported(int64_t N, int64_t Dz, int K, int dtype);
+int tc_router_forward(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, void* alpha,
+                      cudaStream_t st);
+size_t tc_router_backward_ws(int64_t N, int64_t Dz, int K);
+int tc_router_backward(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, const void* alpha,
+                       const void* dalpha, int da_dtype, void* dz, void* dw, void* ws, size_t ws_bytes,
+                       cudaStream_t st);
+
+constexpr int kMaxBasesSimt = 128;
+constexpr int kMaxKernelSize = 64;
+
+}  // namespace moc
