@@ -1,15 +1,632 @@
-// Tensor-core MoC convolution kernels (bf16).  Placeholder until the kernels land.
+// Tensor-core MoC convolution for bf16 x / alpha / basis (sm_100a, mma.sync bf16 -> fp32).
+//
+// The three K-contractions of the operator are small GEMMs per tile:
+//   W[t, s, ch]   = sum_k alpha[t, k] basis[k, s, ch]             (forward, dx, SiLU pre)
+//   dalpha[t, k]  = sum_{s,ch} m[t, s, ch] basis[k, s, ch]        (m = dz * x shifted)
+//   dbasis[k,s,ch]= sum_t alpha[t, k] m[t, s, ch]
+// They run on the tensor cores with fp32 accumulation; the shifts, SiLU and the dz*x
+// products run on the CUDA cores in registers, so the per-token kernel W and the product
+// m never touch memory.  Rounding points follow the reference's bf16 mode
+// (moc/kernels.py:92-95, 125-130, 390-408): alpha, basis and m enter the dots as bf16.
+//
+// Work decomposition: a CTA owns a 128-channel slice and a contiguous range of 64-token
+// work items (fixed-length tiles or the varlen chunks of chunk_indices); 8 warps each own
+// 16 channels.  Tiles are staged in shared memory with cp.async, double buffered.
+//   forward : y = [silu](sum_s W_s * x_shift_s)                       one pass
+//   backward: dz (SiLU pre recomputed on chip), dx, per-slice dalpha partials and per-CTA
+//             dbasis partials in one pass over x, dy, alpha; a second small kernel adds the
+//             partials in a fixed order (deterministic, no atomics).
+#include <algorithm>
+
 #include "moc_common.cuh"
 #include "moc_internal.h"
+#include "moc_mma.cuh"
 
 namespace moc {
-bool tc_conv_supported(const moc_problem&) { return false; }
-int tc_forward(const moc_problem&, const void*, const void*, const void*, void*, cudaStream_t) {
+namespace {
+
+constexpr int kTile = 64;                  // token rows per work item
+constexpr int kBD = 128;                   // channels per CTA
+constexpr int kThreads = 256;              // 8 warps x 16 channels
+constexpr int kRowB = (kBD + 8) * 2;       // bf16 channel row in smem: 272 B (16 B pad: conflict-free ldmatrix)
+constexpr int kDzRowB = (kBD + 8) * 4;     // fp32 dz row: 544 B
+constexpr int kHalo = 8;                   // past-halo rows kept before each tile (S - 1 <= 7)
+constexpr int kFut = 16;                   // future rows kept after each tile (S - 1 <= 7, one 16-row block)
+
+template <int KT, int S, bool ACT, bool BWD>
+struct Layout {
+  static constexpr int KP = KT * 16;                                   // bases padded to the MMA K
+  static constexpr int XR = kHalo + kTile + ((BWD && ACT) ? kFut : 0);  // x rows per stage
+  static constexpr int AR = BWD ? kTile + kFut : kTile;                // alpha rows per stage
+  static constexpr int FR = kTile + kFut;                              // dy rows per stage
+  static constexpr int ARB = (KP + 8) * 2;                             // alpha row bytes (48 / 80)
+  static constexpr int basis_bytes = S * KP * kRowB;
+  static constexpr int x_bytes = XR * kRowB;
+  static constexpr int dy_bytes = BWD ? FR * kRowB : 0;
+  static constexpr int a_bytes = AR * ARB;
+  static constexpr int stage_bytes = x_bytes + dy_bytes + a_bytes;
+  static constexpr int dz_bytes = (BWD && ACT) ? FR * kDzRowB : 0;
+  static constexpr int red_bytes = BWD ? 2 * 8 * 16 * KP * 4 : 0;
+  static constexpr int total = basis_bytes + 2 * stage_bytes + dz_bytes + red_bytes;
+};
+
+struct TcArgs {
+  RowMap rm;
+  int64_t D;
+  int K;
+  const bf16* x;
+  const bf16* alpha;
+  const bf16* basis;
+  const bf16* dy;
+  bf16* out;
+  bf16* dx;
+  float* da_part;  // [n_slices][n_tokens][K]
+  float* db_part;  // [groups][K][S][D]
+  int64_t items_per_group;
+  int64_t n_tokens;
+};
+
+// ------------------------------------------------------------------ staging
+
+template <class L, bool BWD, bool ACT>
+__device__ __forceinline__ void load_basis(const TcArgs& a, char* basis_s, int64_t ch_base, int S) {
+  constexpr int KP = L::KP;
+  for (int idx = threadIdx.x; idx < S * KP * 16; idx += kThreads) {
+    const int row = idx >> 4, chunk = idx & 15;
+    const int s = row / KP, k = row - s * KP;
+    const int64_t ch = ch_base + chunk * 8;
+    const bool ok = k < a.K && ch < a.D;
+    const bf16* src = ok ? a.basis + (static_cast<int64_t>(k) * S + s) * a.D + ch : a.basis;
+    cp_async16(smem_addr(basis_s + row * kRowB + chunk * 16), src, ok ? 16u : 0u);
+  }
+}
+
+template <class L, bool BWD, bool ACT>
+__device__ __forceinline__ void load_tile(const TcArgs& a, char* stage, int64_t ss, int64_t se, int64_t r0,
+                                          int64_t r1, int64_t ch_base) {
+  char* x_s = stage;
+  char* dy_s = stage + L::x_bytes;
+  char* a_s = stage + L::x_bytes + L::dy_bytes;
+  const int64_t x_hi = (BWD && ACT) ? se : r1;
+  for (int idx = threadIdx.x; idx < L::XR * 16; idx += kThreads) {
+    const int row = idx >> 4, chunk = idx & 15;
+    const int64_t tok = r0 - kHalo + row;
+    const int64_t ch = ch_base + chunk * 8;
+    const bool ok = tok >= ss && tok < x_hi && ch < a.D;
+    const bf16* src = ok ? a.x + tok * a.D + ch : a.x;
+    cp_async16(smem_addr(x_s + row * kRowB + chunk * 16), src, ok ? 16u : 0u);
+  }
+  if constexpr (BWD) {
+    for (int idx = threadIdx.x; idx < L::FR * 16; idx += kThreads) {
+      const int row = idx >> 4, chunk = idx & 15;
+      const int64_t tok = r0 + row;
+      const int64_t ch = ch_base + chunk * 8;
+      const bool ok = tok < se && ch < a.D;
+      const bf16* src = ok ? a.dy + tok * a.D + ch : a.dy;
+      cp_async16(smem_addr(dy_s + row * kRowB + chunk * 16), src, ok ? 16u : 0u);
+    }
+  }
+  constexpr int kChunks = L::KP / 8;
+  const int64_t a_hi = BWD ? se : r1;
+  for (int idx = threadIdx.x; idx < L::AR * kChunks; idx += kThreads) {
+    const int row = idx / kChunks, chunk = idx - row * kChunks;
+    const int64_t tok = r0 + row;
+    const bool ok = tok < a_hi && chunk * 8 < a.K;
+    const bf16* src = ok ? a.alpha + tok * a.K + chunk * 8 : a.alpha;
+    cp_async16(smem_addr(a_s + row * L::ARB + chunk * 16), src, ok ? 16u : 0u);
+  }
+}
+
+// lane -> row / column offsets of the four 8x8 matrices of an ldmatrix.x4 covering a
+// 16(rows) x 16(cols) block: matrix i = lane/8 holds rows (i&1)*8.. and cols (i>>1)*8..
+__device__ __forceinline__ int lm_row(int lane) { return (lane & 7) + ((lane >> 3) & 1) * 8; }
+__device__ __forceinline__ int lm_col(int lane) { return (lane >> 4) * 8; }
+
+// ------------------------------------------------------------------ forward
+
+template <int KT, int S, bool ACT>
+__global__ void __launch_bounds__(kThreads) k_tc_fwd(TcArgs a) {
+  using L = Layout<KT, S, ACT, false>;
+  extern __shared__ __align__(128) char smem[];
+  char* basis_s = smem;
+  char* stages = smem + L::basis_bytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int64_t ch_base = static_cast<int64_t>(blockIdx.x) * kBD;
+  const int64_t n_items = a.rm.n_items();
+  const int64_t i0 = static_cast<int64_t>(blockIdx.y) * a.items_per_group;
+  const int64_t i1 = i0 + a.items_per_group < n_items ? i0 + a.items_per_group : n_items;
+  if (i0 >= i1) return;
+
+  load_basis<L, false, ACT>(a, basis_s, ch_base, S);
+  {
+    int64_t ss, se, r0, r1;
+    if (a.rm.item(i0, ss, se, r0, r1)) load_tile<L, false, ACT>(a, stages, ss, se, r0, r1, ch_base);
+  }
+  cp_async_commit();
+
+  uint32_t bw[S][KT][4];  // basis fragments for W = alpha . basis_s (B operand, 2 channel n-tiles)
+  for (int64_t it = i0; it < i1; ++it) {
+    const int cur = static_cast<int>((it - i0) & 1);
+    if (it + 1 < i1) {
+      int64_t ss, se, r0, r1;
+      if (a.rm.item(it + 1, ss, se, r0, r1))
+        load_tile<L, false, ACT>(a, stages + (cur ^ 1) * L::stage_bytes, ss, se, r0, r1, ch_base);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (it == i0) {
+#pragma unroll
+      for (int s = 0; s < S; ++s)
+#pragma unroll
+        for (int kt = 0; kt < KT; ++kt)
+          ldsm_x4_t(smem_addr(basis_s + (s * L::KP + kt * 16 + lm_row(lane)) * kRowB +
+                              (warp * 16 + lm_col(lane)) * 2),
+                    bw[s][kt]);
+    }
+    int64_t ss, se, r0, r1;
+    if (a.rm.item(it, ss, se, r0, r1)) {
+      const char* x_s = stages + cur * L::stage_bytes;
+      const char* a_s = x_s + L::x_bytes;
+      const int rows = static_cast<int>(r1 - r0);
+      for (int b = 0; b < 4 && 16 * b < rows; ++b) {
+        uint32_t af[KT][4];
+#pragma unroll
+        for (int kt = 0; kt < KT; ++kt)
+          ldsm_x4(smem_addr(a_s + (16 * b + lm_row(lane)) * L::ARB + (kt * 16 + lm_col(lane)) * 2), af[kt]);
+        float acc[2][4] = {};
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+          const int j = S - 1 - s;
+          float w[2][4] = {};
+#pragma unroll
+          for (int kt = 0; kt < KT; ++kt) {
+            mma_bf16(w[0], af[kt], bw[s][kt][0], bw[s][kt][1]);
+            mma_bf16(w[1], af[kt], bw[s][kt][2], bw[s][kt][3]);
+          }
+          uint32_t xr[4];
+          ldsm_x4(smem_addr(x_s + (kHalo + 16 * b - j + lm_row(lane)) * kRowB + (warp * 16 + lm_col(lane)) * 2), xr);
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            acc[nt][0] = fmaf(w[nt][0], bf_lo(xr[2 * nt]), acc[nt][0]);
+            acc[nt][1] = fmaf(w[nt][1], bf_hi(xr[2 * nt]), acc[nt][1]);
+            acc[nt][2] = fmaf(w[nt][2], bf_lo(xr[2 * nt + 1]), acc[nt][2]);
+            acc[nt][3] = fmaf(w[nt][3], bf_hi(xr[2 * nt + 1]), acc[nt][3]);
+          }
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int64_t ch = ch_base + warp * 16 + nt * 8 + 2 * q;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int64_t tok = r0 + 16 * b + g + 8 * h;
+            float v0 = acc[nt][2 * h], v1 = acc[nt][2 * h + 1];
+            if (ACT) {
+              v0 = silu_f(v0);
+              v1 = silu_f(v1);
+            }
+            if (tok < r1 && ch < a.D)
+              *reinterpret_cast<uint32_t*>(a.out + tok * a.D + ch) = pack_bf16(v0, v1);
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ backward
+
+template <int KT, int S, bool ACT>
+__global__ void __launch_bounds__(kThreads, 1) k_tc_bwd(TcArgs a) {
+  using L = Layout<KT, S, ACT, true>;
+  constexpr int KP = L::KP;
+  extern __shared__ __align__(128) char smem[];
+  char* basis_s = smem;
+  char* stages = smem + L::basis_bytes;
+  char* dz_s = stages + 2 * L::stage_bytes;
+  float* red_s = reinterpret_cast<float*>(dz_s + L::dz_bytes);  // [2][8 warps][16 rows][KP]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int64_t slice = blockIdx.x;
+  const int64_t ch_base = slice * kBD;
+  const int64_t n_items = a.rm.n_items();
+  const int64_t i0 = static_cast<int64_t>(blockIdx.y) * a.items_per_group;
+  const int64_t i1 = i0 + a.items_per_group < n_items ? i0 + a.items_per_group : n_items;
+  const bool want_dx = a.dx != nullptr;
+
+  float dba[S][2 * KT][4] = {};  // dbasis^T accumulators: (ch g | g+8) x (k 8kn + 2q..)
+
+  if (i0 < i1) {
+    load_basis<L, true, ACT>(a, basis_s, ch_base, S);
+    {
+      int64_t ss, se, r0, r1;
+      if (a.rm.item(i0, ss, se, r0, r1)) load_tile<L, true, ACT>(a, stages, ss, se, r0, r1, ch_base);
+    }
+    cp_async_commit();
+  }
+  int red_buf = 0;
+  const int ch_w = warp * 16;  // this warp's channel offset inside the slice
+
+  for (int64_t it = i0; it < i1; ++it) {
+    const int cur = static_cast<int>((it - i0) & 1);
+    if (it + 1 < i1) {
+      int64_t ss, se, r0, r1;
+      if (a.rm.item(it + 1, ss, se, r0, r1))
+        load_tile<L, true, ACT>(a, stages + (cur ^ 1) * L::stage_bytes, ss, se, r0, r1, ch_base);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    int64_t ss, se, r0, r1;
+    const bool valid = a.rm.item(it, ss, se, r0, r1);
+    const char* x_s = stages + cur * L::stage_bytes;
+    const char* dy_s = x_s + L::x_bytes;
+    const char* a_s = dy_s + L::dy_bytes;
+    const int rows = valid ? static_cast<int>(r1 - r0) : 0;
+
+    // dz in the C-fragment layout at tile-relative row base rb: v[nt][2h + e] is
+    // (row rb + g + 8h, channel ch_w + 8nt + 2q + e).
+    auto load_dz = [&](int rb, float (&v)[2][4]) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = rb + g + 8 * h;
+          const int col = ch_w + nt * 8 + 2 * q;
+          if constexpr (ACT) {
+            const float2 d = *reinterpret_cast<const float2*>(dz_s + row * kDzRowB + col * 4);
+            v[nt][2 * h] = d.x;
+            v[nt][2 * h + 1] = d.y;
+          } else {
+            const uint32_t d = *reinterpret_cast<const uint32_t*>(dy_s + row * kRowB + col * 2);
+            v[nt][2 * h] = bf_lo(d);
+            v[nt][2 * h + 1] = bf_hi(d);
+          }
+        }
+    };
+
+    // W fragments (C layout) for alpha rows starting at tile row ar, tap s.
+    auto w_frag = [&](int ar, int s, float (&w)[2][4]) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[nt][e] = 0.f;
+#pragma unroll
+      for (int kt = 0; kt < KT; ++kt) {
+        uint32_t af[4], bf[4];
+        ldsm_x4(smem_addr(a_s + (ar + lm_row(lane)) * L::ARB + (kt * 16 + lm_col(lane)) * 2), af);
+        ldsm_x4_t(smem_addr(basis_s + (s * KP + kt * 16 + lm_row(lane)) * kRowB + (ch_w + lm_col(lane)) * 2), bf);
+        mma_bf16(w[0], af, bf[0], bf[1]);
+        mma_bf16(w[1], af, bf[2], bf[3]);
+      }
+    };
+
+    if (valid) {
+      // ---- phase 1: dz = dy * silu'(pre) for tile rows 0..79 (the future rows feed dx)
+      if constexpr (ACT) {
+        for (int b = 0; b < 5; ++b) {
+          float pre[2][4] = {};
+          if (16 * b < se - r0) {
+#pragma unroll
+            for (int s = 0; s < S; ++s) {
+              const int j = S - 1 - s;
+              float w[2][4];
+              w_frag(16 * b, s, w);
+              uint32_t xr[4];
+              ldsm_x4(smem_addr(x_s + (kHalo + 16 * b - j + lm_row(lane)) * kRowB + (ch_w + lm_col(lane)) * 2), xr);
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt) {
+                pre[nt][0] = fmaf(w[nt][0], bf_lo(xr[2 * nt]), pre[nt][0]);
+                pre[nt][1] = fmaf(w[nt][1], bf_hi(xr[2 * nt]), pre[nt][1]);
+                pre[nt][2] = fmaf(w[nt][2], bf_lo(xr[2 * nt + 1]), pre[nt][2]);
+                pre[nt][3] = fmaf(w[nt][3], bf_hi(xr[2 * nt + 1]), pre[nt][3]);
+              }
+            }
+          }
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int row = 16 * b + g + 8 * h;
+              const int col = ch_w + nt * 8 + 2 * q;
+              const uint32_t d = *reinterpret_cast<const uint32_t*>(dy_s + row * kRowB + col * 2);
+              float2 o;
+              o.x = bf_lo(d) * dsilu_f(pre[nt][2 * h]);
+              o.y = bf_hi(d) * dsilu_f(pre[nt][2 * h + 1]);
+              *reinterpret_cast<float2*>(dz_s + row * kDzRowB + col * 4) = o;
+            }
+        }
+        __syncwarp();
+      }
+    }
+
+    // ---- phase 2: per 16-row block: dx, m, dalpha, dbasis
+    for (int b = 0; b < 4; ++b) {
+      const bool active = 16 * b < rows;  // uniform across the CTA
+      if (active) {
+        float dzu[2][4];
+        load_dz(16 * b, dzu);
+        uint32_t ab[KT][4];  // alpha as the B operand of dbasis (tokens x bases)
+#pragma unroll
+        for (int kt = 0; kt < KT; ++kt)
+          ldsm_x4_t(smem_addr(a_s + (16 * b + lm_row(lane)) * L::ARB + (kt * 16 + lm_col(lane)) * 2), ab[kt]);
+        float dxa[2][4] = {};
+        float daa[2 * KT][4] = {};
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+          const int j = S - 1 - s;
+          if (want_dx) {
+            float w[2][4], dzs[2][4];
+            w_frag(16 * b + j, s, w);  // W at rows t + j
+            load_dz(16 * b + j, dzs);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) dxa[nt][e] = fmaf(w[nt][e], dzs[nt][e], dxa[nt][e]);
+          }
+          uint32_t xr[4];
+          ldsm_x4(smem_addr(x_s + (kHalo + 16 * b - j + lm_row(lane)) * kRowB + (ch_w + lm_col(lane)) * 2), xr);
+          uint32_t m[4];  // A operand (tokens x channels) of dalpha, rounded to bf16
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int nt = r >> 1, h = r & 1;
+            m[r] = pack_bf16(dzu[nt][2 * h] * bf_lo(xr[r]), dzu[nt][2 * h + 1] * bf_hi(xr[r]));
+          }
+#pragma unroll
+          for (int kt = 0; kt < KT; ++kt) {
+            uint32_t bb[4];
+            ldsm_x4(smem_addr(basis_s + (s * KP + kt * 16 + (lane & 7) + (lane >> 4) * 8) * kRowB +
+                              (ch_w + ((lane >> 3) & 1) * 8) * 2),
+                    bb);
+            mma_bf16(daa[2 * kt], m, bb[0], bb[1]);
+            mma_bf16(daa[2 * kt + 1], m, bb[2], bb[3]);
+          }
+          uint32_t mt[4] = {movm_t(m[0]), movm_t(m[2]), movm_t(m[1]), movm_t(m[3])};
+#pragma unroll
+          for (int kt = 0; kt < KT; ++kt) {
+            mma_bf16(dba[s][2 * kt], mt, ab[kt][0], ab[kt][1]);
+            mma_bf16(dba[s][2 * kt + 1], mt, ab[kt][2], ab[kt][3]);
+          }
+        }
+        if (want_dx) {
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int64_t ch = ch_base + ch_w + nt * 8 + 2 * q;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int64_t tok = r0 + 16 * b + g + 8 * h;
+              if (tok < r1 && ch < a.D)
+                *reinterpret_cast<uint32_t*>(a.dx + tok * a.D + ch) = pack_bf16(dxa[nt][2 * h], dxa[nt][2 * h + 1]);
+            }
+          }
+        }
+        float* red = red_s + (red_buf * 8 + warp) * 16 * KP;
+#pragma unroll
+        for (int kn = 0; kn < 2 * KT; ++kn)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            *reinterpret_cast<float2*>(red + (g + 8 * h) * KP + kn * 8 + 2 * q) =
+                make_float2(daa[kn][2 * h], daa[kn][2 * h + 1]);
+        __syncthreads();
+        const float* rb = red_s + red_buf * 8 * 16 * KP;
+        for (int o = threadIdx.x; o < 16 * KP; o += kThreads) {
+          const int row = o / KP, k = o - row * KP;
+          float sum = 0.f;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) sum += rb[w * 16 * KP + o];
+          const int64_t tok = r0 + 16 * b + row;
+          if (k < a.K && tok < r1) a.da_part[(slice * a.n_tokens + tok) * a.K + k] = sum;
+        }
+        red_buf ^= 1;
+      }
+    }
+    __syncthreads();
+  }
+
+  // dbasis partial of this CTA: db_part[group][k][s][ch]
+  const int64_t grp = blockIdx.y;
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+#pragma unroll
+    for (int kn = 0; kn < 2 * KT; ++kn)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int k = kn * 8 + 2 * q + (e & 1);
+        const int64_t ch = ch_base + ch_w + g + 8 * (e >> 1);
+        if (k < a.K && ch < a.D) a.db_part[((grp * a.K + k) * S + s) * a.D + ch] = dba[s][kn][e];
+      }
+}
+
+// dalpha[i] = sum over channel slices, dbasis[i] = sum over token groups (fixed order).
+__global__ void k_tc_finalize(const float* __restrict__ da_part, int64_t n_slices, int64_t nk, void* dalpha,
+                              int adt, const float* __restrict__ db_part, int64_t groups, int64_t ksd, void* dbasis,
+                              int bdt) {
+  const int64_t total = nk + ksd;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float s = 0.f;
+    if (i < nk) {
+      for (int64_t c = 0; c < n_slices; ++c) s += da_part[c * nk + i];
+      st_any(dalpha, adt, i, s);
+    } else {
+      const int64_t j = i - nk;
+      for (int64_t g = 0; g < groups; ++g) s += db_part[g * ksd + j];
+      st_any(dbasis, bdt, j, s);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+struct Plan {
+  RowMap rm;
+  int64_t slices, groups, ipg;
+};
+
+Plan make_plan(const moc_problem& p, int ctas_per_sm) {
+  Plan pl;
+  pl.rm = make_rowmap(p, kTile);
+  pl.slices = ceil_div(p.dim, kBD);
+  const int64_t items = pl.rm.n_items();
+  const int64_t target = static_cast<int64_t>(sm_count()) * ctas_per_sm;
+  int64_t groups = std::max<int64_t>(1, target / pl.slices);
+  groups = std::min<int64_t>(groups, std::max<int64_t>(items, 1));
+  pl.ipg = std::max<int64_t>(1, ceil_div(items, groups));
+  pl.groups = std::max<int64_t>(1, ceil_div(items, pl.ipg));
+  return pl;
+}
+
+// Raises the dynamic shared-memory limit of `kern` once per device (`configured` is owned
+// by the caller's template instantiation, i.e. one flag set per kernel), so launches
+// captured into a CUDA graph later make no attribute calls.
+template <typename Kern>
+int launch(Kern kern, bool (&configured)[64], dim3 grid, int smem, cudaStream_t st, const TcArgs& args) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return note_cuda(e);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return note_cuda(e);
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  kern<<<grid, kThreads, smem, st>>>(args);
+  note_launch();
+  return note_cuda(cudaGetLastError());
+}
+
+template <int KT, int S, bool ACT>
+int fwd_inst(const moc_problem& p, TcArgs& args, cudaStream_t st) {
+  using L = Layout<KT, S, ACT, false>;
+  const Plan pl = make_plan(p, 3);
+  args.rm = pl.rm;
+  args.items_per_group = pl.ipg;
+  if (pl.rm.n_items() == 0) return MOC_OK;
+  static bool configured[64] = {};
+  return launch(k_tc_fwd<KT, S, ACT>, configured, dim3(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups)),
+                L::total, st, args);
+}
+
+template <int KT, int S, bool ACT>
+int bwd_inst(const moc_problem& p, TcArgs& args, void* dalpha, void* dbasis, cudaStream_t st) {
+  using L = Layout<KT, S, ACT, true>;
+  const Plan pl = make_plan(p, 1);
+  args.rm = pl.rm;
+  args.items_per_group = pl.ipg;
+  const int64_t nk = p.n_tokens * p.n_bases;
+  const int64_t ksd = static_cast<int64_t>(p.n_bases) * p.kernel_size * p.dim;
+  static bool configured[64] = {};
+  int rc = launch(k_tc_bwd<KT, S, ACT>, configured, dim3(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups)),
+                  L::total, st, args);
+  if (rc != MOC_OK) return rc;
+  const int64_t blocks = std::min<int64_t>(ceil_div(nk + ksd, 256), 8 * sm_count());
+  k_tc_finalize<<<static_cast<unsigned>(blocks), 256, 0, st>>>(args.da_part, pl.slices, nk, dalpha, p.alpha_dtype,
+                                                               args.db_part, pl.groups, ksd, dbasis, p.basis_dtype);
+  note_launch();
+  return note_cuda(cudaGetLastError());
+}
+
+template <template <int, int, bool> class F, typename... Args>
+int dispatch(const moc_problem& p, Args&&... args) {
+  const int KT = p.n_bases <= 16 ? 1 : 2;
+  const bool act = p.activation != 0;
+#define MOC_TC_CASE(kt, s)                                                        \
+  if (KT == kt && p.kernel_size == s)                                             \
+    return act ? F<kt, s, true>::run(p, std::forward<Args>(args)...)              \
+               : F<kt, s, false>::run(p, std::forward<Args>(args)...);
+  MOC_TC_CASE(1, 1) MOC_TC_CASE(1, 2) MOC_TC_CASE(1, 3) MOC_TC_CASE(1, 4)
+  MOC_TC_CASE(1, 5) MOC_TC_CASE(1, 6) MOC_TC_CASE(1, 7) MOC_TC_CASE(1, 8)
+  MOC_TC_CASE(2, 1) MOC_TC_CASE(2, 2) MOC_TC_CASE(2, 3) MOC_TC_CASE(2, 4)
+#undef MOC_TC_CASE
   return MOC_ERR_UNSUPPORTED_SHAPE;
 }
-size_t tc_backward_ws(const moc_problem&) { return 0; }
-int tc_backward(const moc_problem&, const void*, const void*, const void*, const void*, void*, void*, void*, void*,
-                size_t, cudaStream_t) {
-  return MOC_ERR_UNSUPPORTED_SHAPE;
+
+template <int KT, int S, bool ACT>
+struct FwdRun {
+  static int run(const moc_problem& p, TcArgs& args, cudaStream_t st) { return fwd_inst<KT, S, ACT>(p, args, st); }
+};
+template <int KT, int S, bool ACT>
+struct BwdRun {
+  static int run(const moc_problem& p, TcArgs& args, void* da, void* db, cudaStream_t st) {
+    return bwd_inst<KT, S, ACT>(p, args, da, db, st);
+  }
+};
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+void ws_split(const moc_problem& p, int64_t& slices, int64_t& groups, size_t& da_bytes, size_t& db_bytes) {
+  const Plan pl = make_plan(p, 1);
+  slices = pl.slices;
+  groups = pl.groups;
+  da_bytes = align_up(static_cast<size_t>(slices * p.n_tokens * p.n_bases) * sizeof(float), 256);
+  db_bytes = align_up(static_cast<size_t>(groups * p.n_bases * p.kernel_size * p.dim) * sizeof(float), 256);
 }
+
+}  // namespace
+
+bool tc_conv_supported(const moc_problem& p) {
+  if (p.x_dtype != MOC_DTYPE_BF16 || p.alpha_dtype != MOC_DTYPE_BF16 || p.basis_dtype != MOC_DTYPE_BF16) return false;
+  if (p.n_bases % 8 != 0 || p.n_bases > 32) return false;
+  if (p.kernel_size < 1 || p.kernel_size > 8) return false;
+  if (p.n_bases > 16 && p.kernel_size > 4) return false;
+  if (p.dim % 8 != 0) return false;
+  if (p.cu_seqlens != nullptr && p.chunk_size != kTile) return false;
+  if (ceil_div(p.dim, kBD) > 65535) return false;
+  return true;
+}
+
+int tc_forward(const moc_problem& p, const void* x, const void* alpha, const void* basis, void* out,
+               cudaStream_t st) {
+  if (!aligned16(x) || !aligned16(alpha) || !aligned16(basis) || !aligned16(out)) return MOC_ERR_MISALIGNED;
+  TcArgs args{};
+  args.D = p.dim;
+  args.K = p.n_bases;
+  args.x = static_cast<const bf16*>(x);
+  args.alpha = static_cast<const bf16*>(alpha);
+  args.basis = static_cast<const bf16*>(basis);
+  args.out = static_cast<bf16*>(out);
+  args.n_tokens = p.n_tokens;
+  return dispatch<FwdRun>(p, args, st);
+}
+
+size_t tc_backward_ws(const moc_problem& p) {
+  int64_t slices, groups;
+  size_t da, db;
+  ws_split(p, slices, groups, da, db);
+  return da + db;
+}
+
+int tc_backward(const moc_problem& p, const void* x, const void* alpha, const void* basis, const void* dy, void* dx,
+                void* dalpha, void* dbasis, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (!aligned16(x) || !aligned16(alpha) || !aligned16(basis) || !aligned16(dy) || (dx && !aligned16(dx)))
+    return MOC_ERR_MISALIGNED;
+  int64_t slices, groups;
+  size_t da, db;
+  ws_split(p, slices, groups, da, db);
+  if (ws_bytes < da + db) return MOC_ERR_WORKSPACE_TOO_SMALL;
+  TcArgs args{};
+  args.D = p.dim;
+  args.K = p.n_bases;
+  args.x = static_cast<const bf16*>(x);
+  args.alpha = static_cast<const bf16*>(alpha);
+  args.basis = static_cast<const bf16*>(basis);
+  args.dy = static_cast<const bf16*>(dy);
+  args.dx = static_cast<bf16*>(dx);
+  args.da_part = static_cast<float*>(ws);
+  args.db_part = reinterpret_cast<float*>(static_cast<char*>(ws) + da);
+  args.n_tokens = p.n_tokens;
+  return dispatch<BwdRun>(p, args, dalpha, dbasis, st);
+}
+
 }  // namespace moc

@@ -103,6 +103,12 @@ def prepare_chunk_indices(
     return table
 
 
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    """Contiguous and 16-byte aligned (the vectorised kernels stage rows in 16 B chunks)."""
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 def _check_chunk_indices(chunk_indices: torch.Tensor, cu_seqlens: torch.Tensor) -> None:
     if not chunk_indices.is_cuda or chunk_indices.device != cu_seqlens.device:
         raise ValueError("chunk_indices must be a CUDA tensor on the same device as cu_seqlens")
@@ -171,9 +177,7 @@ def launch_forward(
     block_t: int = VARLEN_BLOCK_T,
 ) -> torch.Tensor:
     """y = [silu](conv(x, alpha, basis)) in x.dtype (reference: moc/ops.py:129-194)."""
-    x = x.contiguous()
-    alpha = alpha.contiguous()
-    basis = basis.contiguous()
+    x, alpha, basis = _aligned(x), _aligned(alpha), _aligned(basis)
     out = torch.empty_like(x)
     p, keep = _problem(x, alpha, basis, activation_flag, cu_seqlens, cu_seqlens_cpu, chunk_indices, block_t)
     with torch.cuda.device(x.device):
@@ -224,10 +228,7 @@ def launch_backward(
     is reduced deterministically (per-CTA fp32 partials summed in a fixed order).
     """
     del preact
-    x = x.contiguous()
-    alpha = alpha.contiguous()
-    basis = basis.contiguous()
-    moc_dy = moc_dy.contiguous()
+    x, alpha, basis, moc_dy = _aligned(x), _aligned(alpha), _aligned(basis), _aligned(moc_dy)
     p, keep = _problem(x, alpha, basis, activation_flag, cu_seqlens, cu_seqlens_cpu, chunk_indices, block_t)
     lib = _lib.load()
     dx = torch.empty_like(x) if need_x else None

@@ -20,6 +20,8 @@ from oracle import moc_oracle as O
 pytestmark = pytest.mark.gpu
 
 TOL = {torch.float32: 1e-4, torch.bfloat16: 2e-2}
+# an output stored in a narrower dtype than the compute dtype carries that dtype's rounding
+STORE_TOL = {torch.float32: 1e-4, torch.float16: 2e-3, torch.bfloat16: 2e-2}
 DEV = "cuda"
 
 
@@ -49,8 +51,9 @@ def _run(x, a, basis, dy, xdt, adt, bdt, act, cu=None, max_seqlen=None, **kw):
 
 def _assert_close(got, ref, xdt, label):
     for name in ("y", "dx", "dalpha", "dbasis"):
+        tol = max(TOL[xdt], STORE_TOL[got[name].dtype])
         err = rel_err(got[name], ref[name])
-        assert err <= TOL[xdt], f"{label} {name}: rel err {err:.3e} > {TOL[xdt]}"
+        assert err <= tol, f"{label} {name}: rel err {err:.3e} > {tol}"
 
 
 @pytest.fixture(params=[0, 1], ids=["auto", "generic"])
@@ -115,7 +118,7 @@ def test_golden_conv_cases(golden):
         y.backward(dy.to(xdt).to(DEV))
         for name, t in (("y", y), ("dx", kx.grad), ("dalpha", ka.grad), ("dbasis", kb.grad)):
             err = rel_err(t, golden.t(f"conv/{case['name']}/{name}"))
-            assert err <= TOL[xdt], (case["name"], name, err)
+            assert err <= max(TOL[xdt], STORE_TOL[t.dtype]), (case["name"], name, err)
 
 
 # ------------------------------------------------------------- determinism and options
