@@ -1,15 +1,405 @@
-// Tensor-core router kernels (bf16).  Placeholder until the kernels land.
+// Tensor-core router for bf16: alpha = softmax/exp(z @ W^T) and its backward.
+//
+// Replaces the reference's F.linear + torch.softmax / torch.exp and their autograd
+// (moc/api.py:383-388).  The projection [N, Dz] x [Dz, K] is tall and skinny (K <= 32),
+// so both kernels are bound by streaming z (and writing dz) through HBM:
+//
+//   forward : a CTA owns 64 token rows and streams their z rows in 128-column chunks
+//             through a 4-stage cp.async ring; each warp accumulates a 16 x K logit tile
+//             with mma.sync (fp32) and applies softmax (over the 4 lanes of a quad that
+//             hold one row) or exp before writing alpha.  Logits never leave registers.
+//   backward: dlogits = alpha*(dalpha - sum alpha*dalpha) (softmax) or alpha*dalpha (exp),
+//             then dz = dlogits @ W and dW = dlogits^T @ z in one pass over z: a CTA owns a
+//             128-column slice of Dz and a contiguous token range, writes its dz columns and
+//             keeps dW^T for its slice in registers; a second kernel adds the per-CTA dW
+//             partials in a fixed order (deterministic).
+#include <algorithm>
+
 #include "moc_common.cuh"
 #include "moc_internal.h"
+#include "moc_mma.cuh"
 
 namespace moc {
-bool tc_router_supported(int64_t, int64_t, int, int) { return false; }
-int tc_router_forward(int64_t, int64_t, int, int, const void*, const void*, void*, cudaStream_t) {
-  return MOC_ERR_UNSUPPORTED_SHAPE;
+namespace {
+
+constexpr int kZC = 128;             // z columns per chunk / slice
+constexpr int kRowB = (kZC + 8) * 2; // 272 B smem row
+constexpr int kFwdRows = 64;         // tokens per forward CTA
+constexpr int kFwdStages = 4;
+constexpr int kBwdTile = 64;         // tokens per backward tile
+
+__device__ __forceinline__ int lm_row(int lane) { return (lane & 7) + ((lane >> 3) & 1) * 8; }
+__device__ __forceinline__ int lm_col(int lane) { return (lane >> 4) * 8; }
+
+// ------------------------------------------------------------------ forward
+
+template <int KT>
+struct FwdLayout {
+  static constexpr int KP = KT * 16;
+  static constexpr int z_bytes = kFwdRows * kRowB;
+  static constexpr int w_bytes = KP * kRowB;
+  static constexpr int stage_bytes = z_bytes + w_bytes;
+  static constexpr int total = kFwdStages * stage_bytes;
+};
+
+template <int KT>
+__global__ void __launch_bounds__(128) k_router_fwd_tc(const bf16* __restrict__ z, const bf16* __restrict__ w,
+                                                       bf16* __restrict__ alpha, int64_t N, int64_t Dz, int K,
+                                                       int act) {
+  using L = FwdLayout<KT>;
+  extern __shared__ __align__(128) char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kFwdRows;
+  const int n_chunks = static_cast<int>((Dz + kZC - 1) / kZC);
+
+  auto load_chunk = [&](int c) {
+    char* st = smem + (c % kFwdStages) * L::stage_bytes;
+    const int64_t col0 = static_cast<int64_t>(c) * kZC;
+    for (int idx = threadIdx.x; idx < (kFwdRows + L::KP) * 16; idx += 128) {
+      const int row = idx >> 4, chunk = idx & 15;
+      const int64_t col = col0 + chunk * 8;
+      if (row < kFwdRows) {
+        const int64_t tok = t0 + row;
+        const bool ok = tok < N && col < Dz;
+        cp_async16(smem_addr(st + row * kRowB + chunk * 16), ok ? z + tok * Dz + col : z, ok ? 16u : 0u);
+      } else {
+        const int k = row - kFwdRows;
+        const bool ok = k < K && col < Dz;
+        cp_async16(smem_addr(st + L::z_bytes + k * kRowB + chunk * 16), ok ? w + k * Dz + col : w,
+                   ok ? 16u : 0u);
+      }
+    }
+  };
+
+#pragma unroll
+  for (int c = 0; c < kFwdStages - 1; ++c) {
+    if (c < n_chunks) load_chunk(c);
+    cp_async_commit();
+  }
+  float acc[2 * KT][4] = {};
+  for (int c = 0; c < n_chunks; ++c) {
+    cp_async_wait<kFwdStages - 2>();
+    __syncthreads();
+    if (c + kFwdStages - 1 < n_chunks) load_chunk(c + kFwdStages - 1);
+    cp_async_commit();
+    const char* st = smem + (c % kFwdStages) * L::stage_bytes;
+    const char* z_s = st;
+    const char* w_s = st + L::z_bytes;
+#pragma unroll
+    for (int kk = 0; kk < kZC / 16; ++kk) {
+      uint32_t af[4];
+      ldsm_x4(smem_addr(z_s + (warp * 16 + lm_row(lane)) * kRowB + (kk * 16 + lm_col(lane)) * 2), af);
+#pragma unroll
+      for (int kt = 0; kt < KT; ++kt) {
+        uint32_t bb[4];  // (k 0-7 | 8-15) x (dz 0-7 | 8-15) of this 16-base group
+        ldsm_x4(smem_addr(w_s + (kt * 16 + (lane & 7) + (lane >> 4) * 8) * kRowB +
+                          (kk * 16 + ((lane >> 3) & 1) * 8) * 2),
+                bb);
+        mma_bf16(acc[2 * kt], af, bb[0], bb[1]);
+        mma_bf16(acc[2 * kt + 1], af, bb[2], bb[3]);
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  // acc[kn][2h + e] = logit(token warp*16 + g + 8h, base 8kn + 2q + e); the 4 lanes of a
+  // quad hold one token row.
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float mx = -INFINITY;
+    if (act == 0) {
+#pragma unroll
+      for (int kn = 0; kn < 2 * KT; ++kn)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          if (kn * 8 + 2 * q + e < K) mx = fmaxf(mx, acc[kn][2 * h + e]);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    } else {
+      mx = 0.f;
+    }
+    float ev[2 * KT][2];
+    float sum = 0.f;
+#pragma unroll
+    for (int kn = 0; kn < 2 * KT; ++kn)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        ev[kn][e] = kn * 8 + 2 * q + e < K ? expf(acc[kn][2 * h + e] - mx) : 0.f;
+        sum += ev[kn][e];
+      }
+    float inv = 1.f;
+    if (act == 0) {
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      inv = 1.f / sum;
+    }
+    const int64_t tok = t0 + warp * 16 + g + 8 * h;
+    if (tok < N) {
+#pragma unroll
+      for (int kn = 0; kn < 2 * KT; ++kn) {
+        const int k = kn * 8 + 2 * q;
+        if (k < K)
+          *reinterpret_cast<uint32_t*>(alpha + tok * K + k) = pack_bf16(ev[kn][0] * inv, ev[kn][1] * inv);
+      }
+    }
+  }
 }
-size_t tc_router_backward_ws(int64_t, int64_t, int) { return 0; }
-int tc_router_backward(int64_t, int64_t, int, int, const void*, const void*, const void*, const void*, int, void*,
-                       void*, void*, size_t, cudaStream_t) {
-  return MOC_ERR_UNSUPPORTED_SHAPE;
+
+// ------------------------------------------------------------------ backward
+
+template <int KT>
+struct BwdLayout {
+  static constexpr int KP = KT * 16;
+  static constexpr int DLB = (KP + 8) * 2;  // dl row bytes
+  static constexpr int w_bytes = KP * kRowB;
+  static constexpr int z_bytes = kBwdTile * kRowB;
+  static constexpr int dl_bytes = kBwdTile * DLB;
+  static constexpr int total = w_bytes + 2 * z_bytes + dl_bytes;
+};
+
+struct RouterBwdArgs {
+  const bf16* z;
+  const bf16* w;
+  const bf16* alpha;
+  const void* dalpha;
+  int da_dtype;
+  bf16* dz;
+  float* dw_part;  // [groups][K][Dz]
+  int64_t N, Dz;
+  int K, act;
+  int64_t tiles_per_group;
+};
+
+template <int KT>
+__global__ void __launch_bounds__(256) k_router_bwd_tc(RouterBwdArgs a) {
+  using L = BwdLayout<KT>;
+  constexpr int KP = L::KP;
+  extern __shared__ __align__(128) char smem[];
+  char* w_s = smem;
+  char* z_st = smem + L::w_bytes;
+  char* dl_s = z_st + 2 * L::z_bytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int64_t col_base = static_cast<int64_t>(blockIdx.x) * kZC;
+  const int64_t n_tiles = (a.N + kBwdTile - 1) / kBwdTile;
+  const int64_t i0 = static_cast<int64_t>(blockIdx.y) * a.tiles_per_group;
+  const int64_t i1 = i0 + a.tiles_per_group < n_tiles ? i0 + a.tiles_per_group : n_tiles;
+  const int cw = warp * 16;  // this warp's 16 columns inside the slice
+  const bool want_dz = a.dz != nullptr;
+  const bool want_dw = a.dw_part != nullptr;
+
+  auto load_z = [&](int64_t tile, char* dst) {
+    for (int idx = threadIdx.x; idx < kBwdTile * 16; idx += 256) {
+      const int row = idx >> 4, chunk = idx & 15;
+      const int64_t tok = tile * kBwdTile + row;
+      const int64_t col = col_base + chunk * 8;
+      const bool ok = tok < a.N && col < a.Dz;
+      cp_async16(smem_addr(dst + row * kRowB + chunk * 16), ok ? a.z + tok * a.Dz + col : a.z, ok ? 16u : 0u);
+    }
+  };
+
+  float dwa[2 * KT][4] = {};  // dW^T: (column cw + g | +8) x (base 8kn + 2q..)
+  if (i0 < i1) {
+    for (int idx = threadIdx.x; idx < KP * 16; idx += 256) {
+      const int k = idx >> 4, chunk = idx & 15;
+      const int64_t col = col_base + chunk * 8;
+      const bool ok = k < a.K && col < a.Dz;
+      cp_async16(smem_addr(w_s + k * kRowB + chunk * 16), ok ? a.w + k * a.Dz + col : a.w, ok ? 16u : 0u);
+    }
+    load_z(i0, z_st);
+    cp_async_commit();
+  }
+  for (int64_t it = i0; it < i1; ++it) {
+    const int cur = static_cast<int>((it - i0) & 1);
+    // dlogits for this tile's 64 tokens (bf16, like the reference's bf16 autograd)
+    if (threadIdx.x < kBwdTile) {
+      const int64_t tok = it * kBwdTile + threadIdx.x;
+      bf16* row = reinterpret_cast<bf16*>(dl_s + threadIdx.x * L::DLB);
+      if (tok < a.N) {
+        float dot = 0.f;
+        if (a.act == 0)
+          for (int k = 0; k < a.K; ++k)
+            dot += __bfloat162float(a.alpha[tok * a.K + k]) * ld_any(a.dalpha, a.da_dtype, tok * a.K + k);
+        for (int k = 0; k < KP; ++k) {
+          float v = 0.f;
+          if (k < a.K)
+            v = __bfloat162float(a.alpha[tok * a.K + k]) * (ld_any(a.dalpha, a.da_dtype, tok * a.K + k) - dot);
+          row[k] = __float2bfloat16_rn(v);
+        }
+      } else {
+        for (int k = 0; k < KP; ++k) row[k] = __float2bfloat16_rn(0.f);
+      }
+    }
+    if (it + 1 < i1) {
+      load_z(it + 1, z_st + (cur ^ 1) * L::z_bytes);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const char* z_s = z_st + cur * L::z_bytes;
+    const int64_t tok0 = it * kBwdTile;
+    for (int b = 0; b < kBwdTile / 16; ++b) {
+      if (tok0 + 16 * b >= a.N) break;
+      if (want_dz) {
+        // dz[tok, col] = sum_k dl[tok, k] W[k, col]
+        float acc[2][4] = {};
+#pragma unroll
+        for (int kt = 0; kt < KT; ++kt) {
+          uint32_t af[4], bf[4];
+          ldsm_x4(smem_addr(dl_s + (16 * b + lm_row(lane)) * L::DLB + (kt * 16 + lm_col(lane)) * 2), af);
+          ldsm_x4_t(smem_addr(w_s + (kt * 16 + lm_row(lane)) * kRowB + (cw + lm_col(lane)) * 2), bf);
+          mma_bf16(acc[0], af, bf[0], bf[1]);
+          mma_bf16(acc[1], af, bf[2], bf[3]);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int64_t col = col_base + cw + nt * 8 + 2 * q;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int64_t tok = tok0 + 16 * b + g + 8 * h;
+            if (tok < a.N && col < a.Dz)
+              *reinterpret_cast<uint32_t*>(a.dz + tok * a.Dz + col) = pack_bf16(acc[nt][2 * h], acc[nt][2 * h + 1]);
+          }
+        }
+      }
+      if (want_dw) {
+        // dW^T[col, k] += sum_tok z[tok, col] dl[tok, k]
+        uint32_t zt[4];
+        ldsm_x4_t(smem_addr(z_s + (16 * b + (lane & 7) + (lane >> 4) * 8) * kRowB + (cw + ((lane >> 3) & 1) * 8) * 2),
+                  zt);
+#pragma unroll
+        for (int kt = 0; kt < KT; ++kt) {
+          uint32_t db[4];
+          ldsm_x4_t(smem_addr(dl_s + (16 * b + lm_row(lane)) * L::DLB + (kt * 16 + lm_col(lane)) * 2), db);
+          mma_bf16(dwa[2 * kt], zt, db[0], db[1]);
+          mma_bf16(dwa[2 * kt + 1], zt, db[2], db[3]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (want_dw) {
+    const int64_t grp = blockIdx.y;
+#pragma unroll
+    for (int kn = 0; kn < 2 * KT; ++kn)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int k = kn * 8 + 2 * q + (e & 1);
+        const int64_t col = col_base + cw + g + 8 * (e >> 1);
+        if (k < a.K && col < a.Dz) a.dw_part[(grp * a.K + k) * a.Dz + col] = dwa[kn][e];
+      }
+  }
 }
+
+__global__ void k_sum_groups(const float* __restrict__ part, int64_t groups, int64_t n, void* out, int dtype) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float s = 0.f;
+    for (int64_t g = 0; g < groups; ++g) s += part[g * n + i];
+    st_any(out, dtype, i, s);
+  }
+}
+
+int sm_count_r() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+void bwd_plan(int64_t N, int64_t Dz, int64_t& slices, int64_t& groups, int64_t& tpg) {
+  slices = ceil_div(Dz, kZC);
+  const int64_t tiles = std::max<int64_t>(1, ceil_div(N, kBwdTile));
+  const int64_t target = static_cast<int64_t>(sm_count_r()) * 3;
+  groups = std::min<int64_t>(tiles, std::max<int64_t>(1, target / slices));
+  tpg = ceil_div(tiles, groups);
+  groups = ceil_div(tiles, tpg);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int set_smem(const void* kern, bool (&configured)[64], int smem) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return note_cuda(e);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return note_cuda(e);
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  return MOC_OK;
+}
+
+template <int KT>
+int fwd_kt(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, void* alpha, cudaStream_t st) {
+  static bool configured[64] = {};
+  int rc = set_smem(reinterpret_cast<const void*>(k_router_fwd_tc<KT>), configured, FwdLayout<KT>::total);
+  if (rc != MOC_OK) return rc;
+  k_router_fwd_tc<KT><<<static_cast<unsigned>(ceil_div(N, kFwdRows)), 128, FwdLayout<KT>::total, st>>>(
+      static_cast<const bf16*>(z), static_cast<const bf16*>(w), static_cast<bf16*>(alpha), N, Dz, K, act);
+  note_launch();
+  return note_cuda(cudaGetLastError());
+}
+
+template <int KT>
+int bwd_kt(RouterBwdArgs& a, int64_t slices, int64_t groups, void* dw, cudaStream_t st) {
+  static bool configured[64] = {};
+  int rc = set_smem(reinterpret_cast<const void*>(k_router_bwd_tc<KT>), configured, BwdLayout<KT>::total);
+  if (rc != MOC_OK) return rc;
+  k_router_bwd_tc<KT><<<dim3(static_cast<unsigned>(slices), static_cast<unsigned>(groups)), 256,
+                        BwdLayout<KT>::total, st>>>(a);
+  note_launch();
+  if (dw != nullptr) {
+    const int64_t n = static_cast<int64_t>(a.K) * a.Dz;
+    const int64_t blocks = std::min<int64_t>(ceil_div(n, 256), 4 * sm_count_r());
+    k_sum_groups<<<static_cast<unsigned>(blocks), 256, 0, st>>>(a.dw_part, groups, n, dw, MOC_DTYPE_BF16);
+    note_launch();
+  }
+  return note_cuda(cudaGetLastError());
+}
+
+}  // namespace
+
+bool tc_router_supported(int64_t N, int64_t Dz, int K, int dtype) {
+  return dtype == MOC_DTYPE_BF16 && K % 8 == 0 && K <= 32 && Dz % 8 == 0 && N > 0 && ceil_div(Dz, kZC) <= 65535;
+}
+
+int tc_router_forward(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, void* alpha,
+                      cudaStream_t st) {
+  if (!aligned16(z) || !aligned16(w) || (reinterpret_cast<uintptr_t>(alpha) & 3u)) return MOC_ERR_MISALIGNED;
+  return K <= 16 ? fwd_kt<1>(N, Dz, K, act, z, w, alpha, st) : fwd_kt<2>(N, Dz, K, act, z, w, alpha, st);
+}
+
+size_t tc_router_backward_ws(int64_t N, int64_t Dz, int K) {
+  int64_t slices, groups, tpg;
+  bwd_plan(N, Dz, slices, groups, tpg);
+  return align_up(static_cast<size_t>(groups * K * Dz) * sizeof(float), 256);
+}
+
+int tc_router_backward(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, const void* alpha,
+                       const void* dalpha, int da_dtype, void* dz, void* dw, void* ws, size_t ws_bytes,
+                       cudaStream_t st) {
+  if (!aligned16(z) || !aligned16(w) || (dz && (reinterpret_cast<uintptr_t>(dz) & 3u))) return MOC_ERR_MISALIGNED;
+  if (ws_bytes < tc_router_backward_ws(N, Dz, K)) return MOC_ERR_WORKSPACE_TOO_SMALL;
+  if (dz == nullptr && dw == nullptr) return MOC_OK;
+  RouterBwdArgs a{};
+  a.z = static_cast<const bf16*>(z);
+  a.w = static_cast<const bf16*>(w);
+  a.alpha = static_cast<const bf16*>(alpha);
+  a.dalpha = dalpha;
+  a.da_dtype = da_dtype;
+  a.dz = static_cast<bf16*>(dz);
+  a.dw_part = dw != nullptr ? static_cast<float*>(ws) : nullptr;
+  a.N = N;
+  a.Dz = Dz;
+  a.K = K;
+  a.act = act;
+  int64_t slices, groups, tpg;
+  bwd_plan(N, Dz, slices, groups, tpg);
+  a.tiles_per_group = tpg;
+  return K <= 16 ? bwd_kt<1>(a, slices, groups, dw, st) : bwd_kt<2>(a, slices, groups, dw, st);
+}
+
 }  // namespace moc
