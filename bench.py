@@ -75,7 +75,7 @@ def measured_peaks() -> dict:
 # ----------------------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML every ~20 ms in a thread."""
+    """Samples SM clock and throttle reasons through NVML every ~2 ms in a thread."""
 
     REASONS = {
         "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
@@ -108,7 +108,7 @@ class ClockSampler:
                 self.samples.append((time.perf_counter(), mhz, reasons))
             except Exception:  # noqa: BLE001
                 pass
-            time.sleep(0.02)
+            time.sleep(0.002)
 
     def start(self) -> None:
         if self._nvml is not None:
@@ -180,6 +180,22 @@ def time_region(fn, steps: int, stream: torch.cuda.Stream) -> float:
     end.record(stream)
     torch.cuda.synchronize()
     return start.elapsed_time(end) / steps
+
+
+def graph_time(fn, reps: int, device: torch.device) -> float:
+    """Device time in ms of one fn() call: `reps` calls captured in one CUDA graph and
+    replayed, so host launch overhead is excluded (CUDA events on the replay stream)."""
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    stream = torch.cuda.current_stream(device)
+    g.replay()
+    ms = time_region(g.replay, 3, stream) / reps
+    del g
+    return ms
 
 
 def max_over_ranks(v: float, world: int) -> float:
@@ -364,8 +380,7 @@ def main() -> None:
     kernel_ms = {}
     reps = max(5, min(args.steps, 20))
     for name, fn in kernel_calls.items():
-        fn()
-        kernel_ms[name] = time_region(fn, reps, stream)
+        kernel_ms[name] = graph_time(fn, reps, device)
     dominant = max(kernel_ms, key=kernel_ms.get)
     peaks = measured_peaks()
     kbytes = KERNEL_BYTES_PER_TOKEN[dominant](cfg) * N_rank

@@ -212,24 +212,28 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(RouterBwdArgs a) {
   }
   for (int64_t it = i0; it < i1; ++it) {
     const int cur = static_cast<int>((it - i0) & 1);
-    // dlogits for this tile's 64 tokens (bf16, like the reference's bf16 autograd)
-    if (threadIdx.x < kBwdTile) {
-      const int64_t tok = it * kBwdTile + threadIdx.x;
-      bf16* row = reinterpret_cast<bf16*>(dl_s + threadIdx.x * L::DLB);
-      if (tok < a.N) {
-        float dot = 0.f;
-        if (a.act == 0)
-          for (int k = 0; k < a.K; ++k)
-            dot += __bfloat162float(a.alpha[tok * a.K + k]) * ld_any(a.dalpha, a.da_dtype, tok * a.K + k);
-        for (int k = 0; k < KP; ++k) {
-          float v = 0.f;
-          if (k < a.K)
-            v = __bfloat162float(a.alpha[tok * a.K + k]) * (ld_any(a.dalpha, a.da_dtype, tok * a.K + k) - dot);
-          row[k] = __float2bfloat16_rn(v);
-        }
-      } else {
-        for (int k = 0; k < KP; ++k) row[k] = __float2bfloat16_rn(0.f);
+    // dlogits for this tile's 64 tokens (bf16, like the reference's bf16 autograd): four
+    // threads per token, each owning KP/4 bases; the softmax dot is a quad reduction.
+    {
+      constexpr int KQ = KP / 4;
+      const int row = threadIdx.x >> 2, part = threadIdx.x & 3;
+      const int64_t tok = it * kBwdTile + row;
+      float av[KQ], dv[KQ];
+      float dot = 0.f;
+#pragma unroll
+      for (int e = 0; e < KQ; ++e) {
+        const int k = part * KQ + e;
+        const bool ok = tok < a.N && k < a.K;
+        av[e] = ok ? __bfloat162float(a.alpha[tok * a.K + k]) : 0.f;
+        dv[e] = ok ? ld_any(a.dalpha, a.da_dtype, tok * a.K + k) : 0.f;
+        dot = fmaf(av[e], dv[e], dot);
       }
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+      if (a.act != 0) dot = 0.f;
+      bf16* dst = reinterpret_cast<bf16*>(dl_s + row * L::DLB) + part * KQ;
+#pragma unroll
+      for (int e = 0; e < KQ; ++e) dst[e] = __float2bfloat16_rn(av[e] * (dv[e] - dot));
     }
     if (it + 1 < i1) {
       load_z(it + 1, z_st + (cur ^ 1) * L::z_bytes);

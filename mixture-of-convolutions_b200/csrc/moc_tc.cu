@@ -36,18 +36,27 @@ constexpr int kFut = 16;                   // future rows kept after each tile (
 template <int KT, int S, bool ACT, bool BWD>
 struct Layout {
   static constexpr int KP = KT * 16;                                   // bases padded to the MMA K
+  // basis fragments live in registers when they fit (<= 4 (tap, 16-base) groups)
+  static constexpr bool BREG = KT * S <= 4;
   static constexpr int XR = kHalo + kTile + ((BWD && ACT) ? kFut : 0);  // x rows per stage
-  static constexpr int AR = BWD ? kTile + kFut : kTile;                // alpha rows per stage
-  static constexpr int FR = kTile + kFut;                              // dy rows per stage
+  // rows of dy / alpha after the tile start: the dx taps read up to S-1 <= 7 future rows;
+  // with SiLU the pre-activation of those rows is one more 16-row MMA block.
+  static constexpr int FR = BWD ? (ACT ? kTile + kFut : kTile + 8) : 0;
+  static constexpr int AR = BWD ? (ACT ? kTile + kFut : kTile + 8) : kTile;
   static constexpr int ARB = (KP + 8) * 2;                             // alpha row bytes (48 / 80)
   static constexpr int basis_bytes = S * KP * kRowB;
   static constexpr int x_bytes = XR * kRowB;
-  static constexpr int dy_bytes = BWD ? FR * kRowB : 0;
+  static constexpr int dy_bytes = FR * kRowB;
   static constexpr int a_bytes = AR * ARB;
   static constexpr int stage_bytes = x_bytes + dy_bytes + a_bytes;
   static constexpr int dz_bytes = (BWD && ACT) ? FR * kDzRowB : 0;
   static constexpr int red_bytes = BWD ? 2 * 8 * 16 * KP * 4 : 0;
-  static constexpr int total = basis_bytes + 2 * stage_bytes + dz_bytes + red_bytes;
+  // with register-resident basis fragments the basis staging area is reused for the
+  // dalpha reduction buffer once the fragments are loaded
+  static constexpr int head_bytes = (BWD && BREG) ? (basis_bytes > red_bytes ? basis_bytes : red_bytes)
+                                                  : basis_bytes + red_bytes;
+  static constexpr int total = head_bytes + 2 * stage_bytes + dz_bytes;
+  static constexpr int min_blocks = BWD ? ((BREG && !ACT && KT == 1) ? 2 : 1) : (KT == 1 ? 3 : 2);
 };
 
 struct TcArgs {
@@ -125,11 +134,11 @@ __device__ __forceinline__ int lm_col(int lane) { return (lane >> 4) * 8; }
 // ------------------------------------------------------------------ forward
 
 template <int KT, int S, bool ACT>
-__global__ void __launch_bounds__(kThreads) k_tc_fwd(TcArgs a) {
+__global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_blocks)) k_tc_fwd(TcArgs a) {
   using L = Layout<KT, S, ACT, false>;
   extern __shared__ __align__(128) char smem[];
   char* basis_s = smem;
-  char* stages = smem + L::basis_bytes;
+  char* stages = smem + L::head_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int64_t ch_base = static_cast<int64_t>(blockIdx.x) * kBD;
@@ -144,6 +153,11 @@ __global__ void __launch_bounds__(kThreads) k_tc_fwd(TcArgs a) {
     if (a.rm.item(i0, ss, se, r0, r1)) load_tile<L, false, ACT>(a, stages, ss, se, r0, r1, ch_base);
   }
   cp_async_commit();
+
+  // per-lane shared-memory offsets of the ldmatrix row addresses
+  const uint32_t a_lane = static_cast<uint32_t>(lm_row(lane) * L::ARB + lm_col(lane) * 2);
+  const uint32_t x_lane = static_cast<uint32_t>(lm_row(lane) * kRowB + (warp * 16 + lm_col(lane)) * 2);
+  const int64_t ch_out = ch_base + warp * 16 + 2 * q;
 
   uint32_t bw[S][KT][4];  // basis fragments for W = alpha . basis_s (B operand, 2 channel n-tiles)
   for (int64_t it = i0; it < i1; ++it) {
@@ -169,14 +183,16 @@ __global__ void __launch_bounds__(kThreads) k_tc_fwd(TcArgs a) {
     }
     int64_t ss, se, r0, r1;
     if (a.rm.item(it, ss, se, r0, r1)) {
-      const char* x_s = stages + cur * L::stage_bytes;
-      const char* a_s = x_s + L::x_bytes;
+      const uint32_t x_s = smem_addr(stages + cur * L::stage_bytes);
+      const uint32_t a_s = x_s + L::x_bytes;
       const int rows = static_cast<int>(r1 - r0);
-      for (int b = 0; b < 4 && 16 * b < rows; ++b) {
+      const int nb = (rows + 15) >> 4;
+      bf16* out_row = a.out + (r0 + g) * a.D + ch_out;
+#pragma unroll 1
+      for (int b = 0; b < nb; ++b) {
         uint32_t af[KT][4];
 #pragma unroll
-        for (int kt = 0; kt < KT; ++kt)
-          ldsm_x4(smem_addr(a_s + (16 * b + lm_row(lane)) * L::ARB + (kt * 16 + lm_col(lane)) * 2), af[kt]);
+        for (int kt = 0; kt < KT; ++kt) ldsm_x4(a_s + (16 * b) * L::ARB + kt * 32 + a_lane, af[kt]);
         float acc[2][4] = {};
 #pragma unroll
         for (int s = 0; s < S; ++s) {
@@ -188,28 +204,25 @@ __global__ void __launch_bounds__(kThreads) k_tc_fwd(TcArgs a) {
             mma_bf16(w[1], af[kt], bw[s][kt][2], bw[s][kt][3]);
           }
           uint32_t xr[4];
-          ldsm_x4(smem_addr(x_s + (kHalo + 16 * b - j + lm_row(lane)) * kRowB + (warp * 16 + lm_col(lane)) * 2), xr);
+          ldsm_x4(x_s + (kHalo + 16 * b - j) * kRowB + x_lane, xr);
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
-            acc[nt][0] = fmaf(w[nt][0], bf_lo(xr[2 * nt]), acc[nt][0]);
-            acc[nt][1] = fmaf(w[nt][1], bf_hi(xr[2 * nt]), acc[nt][1]);
-            acc[nt][2] = fmaf(w[nt][2], bf_lo(xr[2 * nt + 1]), acc[nt][2]);
-            acc[nt][3] = fmaf(w[nt][3], bf_hi(xr[2 * nt + 1]), acc[nt][3]);
+            ffma2(acc[nt][0], acc[nt][1], w[nt][0], w[nt][1], bf_lo(xr[2 * nt]), bf_hi(xr[2 * nt]));
+            ffma2(acc[nt][2], acc[nt][3], w[nt][2], w[nt][3], bf_lo(xr[2 * nt + 1]), bf_hi(xr[2 * nt + 1]));
           }
         }
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int64_t ch = ch_base + warp * 16 + nt * 8 + 2 * q;
+        for (int h = 0; h < 2; ++h) {
+          const bool row_ok = 16 * b + g + 8 * h < rows;
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int64_t tok = r0 + 16 * b + g + 8 * h;
+          for (int nt = 0; nt < 2; ++nt) {
             float v0 = acc[nt][2 * h], v1 = acc[nt][2 * h + 1];
             if (ACT) {
               v0 = silu_f(v0);
               v1 = silu_f(v1);
             }
-            if (tok < r1 && ch < a.D)
-              *reinterpret_cast<uint32_t*>(a.out + tok * a.D + ch) = pack_bf16(v0, v1);
+            if (row_ok && ch_out + nt * 8 < a.D)
+              *reinterpret_cast<uint32_t*>(out_row + (16 * b + 8 * h) * a.D + nt * 8) = pack_bf16(v0, v1);
           }
         }
       }
@@ -221,14 +234,15 @@ __global__ void __launch_bounds__(kThreads) k_tc_fwd(TcArgs a) {
 // ------------------------------------------------------------------ backward
 
 template <int KT, int S, bool ACT>
-__global__ void __launch_bounds__(kThreads, 1) k_tc_bwd(TcArgs a) {
+__global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_blocks)) k_tc_bwd(TcArgs a) {
   using L = Layout<KT, S, ACT, true>;
   constexpr int KP = L::KP;
+  constexpr bool BREG = L::BREG;
   extern __shared__ __align__(128) char smem[];
   char* basis_s = smem;
-  char* stages = smem + L::basis_bytes;
+  float* red_s = reinterpret_cast<float*>(smem + (BREG ? 0 : L::basis_bytes));  // [2][8 warps][16][KP]
+  char* stages = smem + L::head_bytes;
   char* dz_s = stages + 2 * L::stage_bytes;
-  float* red_s = reinterpret_cast<float*>(dz_s + L::dz_bytes);  // [2][8 warps][16 rows][KP]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int64_t slice = blockIdx.x;
@@ -237,8 +251,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_bwd(TcArgs a) {
   const int64_t i0 = static_cast<int64_t>(blockIdx.y) * a.items_per_group;
   const int64_t i1 = i0 + a.items_per_group < n_items ? i0 + a.items_per_group : n_items;
   const bool want_dx = a.dx != nullptr;
+  const int ch_w = warp * 16;  // this warp's channel offset inside the slice
 
-  float dba[S][2 * KT][4] = {};  // dbasis^T accumulators: (ch g | g+8) x (k 8kn + 2q..)
+  // per-lane shared-memory offsets of ldmatrix row addresses
+  const uint32_t basis_base = smem_addr(basis_s);
+  const uint32_t a_lane = static_cast<uint32_t>(lm_row(lane) * L::ARB + lm_col(lane) * 2);
+  const uint32_t c_lane = static_cast<uint32_t>(lm_row(lane) * kRowB + (ch_w + lm_col(lane)) * 2);
+  const uint32_t bt_lane = static_cast<uint32_t>(lm_row(lane) * kRowB + (ch_w + lm_col(lane)) * 2);
+  const uint32_t bn_lane =
+      static_cast<uint32_t>(((lane & 7) + (lane >> 4) * 8) * kRowB + (ch_w + ((lane >> 3) & 1) * 8) * 2);
+
+  float dba[S][2 * KT][4] = {};              // dbasis^T accumulators: (ch g | g+8) x (k 8kn + 2q..)
+  uint32_t bw[BREG ? S : 1][KT][4];          // basis, B operand of W = alpha . basis_s
+  uint32_t bd[BREG ? S : 1][KT][4];          // basis^T, B operand of dalpha = m . basis_s^T
 
   if (i0 < i1) {
     load_basis<L, true, ACT>(a, basis_s, ch_base, S);
@@ -249,7 +274,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_bwd(TcArgs a) {
     cp_async_commit();
   }
   int red_buf = 0;
-  const int ch_w = warp * 16;  // this warp's channel offset inside the slice
 
   for (int64_t it = i0; it < i1; ++it) {
     const int cur = static_cast<int>((it - i0) & 1);
@@ -263,33 +287,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_bwd(TcArgs a) {
       cp_async_wait<0>();
     }
     __syncthreads();
+    if constexpr (BREG) {
+      if (it == i0) {
+#pragma unroll
+        for (int s = 0; s < (BREG ? S : 1); ++s)
+#pragma unroll
+          for (int kt = 0; kt < KT; ++kt) {
+            ldsm_x4_t(basis_base + (s * KP + kt * 16) * kRowB + bt_lane, bw[s][kt]);
+            ldsm_x4(basis_base + (s * KP + kt * 16) * kRowB + bn_lane, bd[s][kt]);
+          }
+        __syncthreads();  // the basis area becomes the dalpha reduction buffer
+      }
+    }
     int64_t ss, se, r0, r1;
     const bool valid = a.rm.item(it, ss, se, r0, r1);
-    const char* x_s = stages + cur * L::stage_bytes;
-    const char* dy_s = x_s + L::x_bytes;
-    const char* a_s = dy_s + L::dy_bytes;
+    const uint32_t x_s = smem_addr(stages + cur * L::stage_bytes);
+    const uint32_t dy_s = x_s + L::x_bytes;
+    const uint32_t a_s = dy_s + L::dy_bytes;
+    const char* dy_p = stages + cur * L::stage_bytes + L::x_bytes;
     const int rows = valid ? static_cast<int>(r1 - r0) : 0;
-
-    // dz in the C-fragment layout at tile-relative row base rb: v[nt][2h + e] is
-    // (row rb + g + 8h, channel ch_w + 8nt + 2q + e).
-    auto load_dz = [&](int rb, float (&v)[2][4]) {
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int row = rb + g + 8 * h;
-          const int col = ch_w + nt * 8 + 2 * q;
-          if constexpr (ACT) {
-            const float2 d = *reinterpret_cast<const float2*>(dz_s + row * kDzRowB + col * 4);
-            v[nt][2 * h] = d.x;
-            v[nt][2 * h + 1] = d.y;
-          } else {
-            const uint32_t d = *reinterpret_cast<const uint32_t*>(dy_s + row * kRowB + col * 2);
-            v[nt][2 * h] = bf_lo(d);
-            v[nt][2 * h + 1] = bf_hi(d);
-          }
-        }
-    };
 
     // W fragments (C layout) for alpha rows starting at tile row ar, tap s.
     auto w_frag = [&](int ar, int s, float (&w)[2][4]) {
@@ -299,16 +315,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_bwd(TcArgs a) {
         for (int e = 0; e < 4; ++e) w[nt][e] = 0.f;
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt) {
-        uint32_t af[4], bf[4];
-        ldsm_x4(smem_addr(a_s + (ar + lm_row(lane)) * L::ARB + (kt * 16 + lm_col(lane)) * 2), af);
-        ldsm_x4_t(smem_addr(basis_s + (s * KP + kt * 16 + lm_row(lane)) * kRowB + (ch_w + lm_col(lane)) * 2), bf);
-        mma_bf16(w[0], af, bf[0], bf[1]);
-        mma_bf16(w[1], af, bf[2], bf[3]);
+        uint32_t af[4];
+        ldsm_x4(a_s + ar * L::ARB + kt * 32 + a_lane, af);
+        if constexpr (BREG) {
+          mma_bf16(w[0], af, bw[s][kt][0], bw[s][kt][1]);
+          mma_bf16(w[1], af, bw[s][kt][2], bw[s][kt][3]);
+        } else {
+          uint32_t bf[4];
+          ldsm_x4_t(basis_base + (s * KP + kt * 16) * kRowB + bt_lane, bf);
+          mma_bf16(w[0], af, bf[0], bf[1]);
+          mma_bf16(w[1], af, bf[2], bf[3]);
+        }
       }
+    };
+    // fp32 dz (SiLU path) in the C layout: v[nt][2h + e] at (row rb + g + 8h, ch 8nt + 2q + e)
+    auto load_dz32 = [&](int rb, float (&v)[2][4]) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float2 d = *reinterpret_cast<const float2*>(dz_s + (rb + g + 8 * h) * kDzRowB +
+                                                            (ch_w + nt * 8 + 2 * q) * 4);
+          v[nt][2 * h] = d.x;
+          v[nt][2 * h + 1] = d.y;
+        }
     };
 
     if (valid) {
-      // ---- phase 1: dz = dy * silu'(pre) for tile rows 0..79 (the future rows feed dx)
+      // ---- phase 1 (SiLU): dz = dy * silu'(pre) for tile rows 0..79 (future rows feed dx)
       if constexpr (ACT) {
         for (int b = 0; b < 5; ++b) {
           float pre[2][4] = {};
@@ -319,13 +353,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_bwd(TcArgs a) {
               float w[2][4];
               w_frag(16 * b, s, w);
               uint32_t xr[4];
-              ldsm_x4(smem_addr(x_s + (kHalo + 16 * b - j + lm_row(lane)) * kRowB + (ch_w + lm_col(lane)) * 2), xr);
+              ldsm_x4(x_s + (kHalo + 16 * b - j) * kRowB + c_lane, xr);
 #pragma unroll
               for (int nt = 0; nt < 2; ++nt) {
-                pre[nt][0] = fmaf(w[nt][0], bf_lo(xr[2 * nt]), pre[nt][0]);
-                pre[nt][1] = fmaf(w[nt][1], bf_hi(xr[2 * nt]), pre[nt][1]);
-                pre[nt][2] = fmaf(w[nt][2], bf_lo(xr[2 * nt + 1]), pre[nt][2]);
-                pre[nt][3] = fmaf(w[nt][3], bf_hi(xr[2 * nt + 1]), pre[nt][3]);
+                ffma2(pre[nt][0], pre[nt][1], w[nt][0], w[nt][1], bf_lo(xr[2 * nt]), bf_hi(xr[2 * nt]));
+                ffma2(pre[nt][2], pre[nt][3], w[nt][2], w[nt][3], bf_lo(xr[2 * nt + 1]), bf_hi(xr[2 * nt + 1]));
               }
             }
           }
@@ -335,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_bwd(TcArgs a) {
             for (int h = 0; h < 2; ++h) {
               const int row = 16 * b + g + 8 * h;
               const int col = ch_w + nt * 8 + 2 * q;
-              const uint32_t d = *reinterpret_cast<const uint32_t*>(dy_s + row * kRowB + col * 2);
+              const uint32_t d = *reinterpret_cast<const uint32_t*>(dy_p + row * kRowB + col * 2);
               float2 o;
               o.x = bf_lo(d) * dsilu_f(pre[nt][2 * h]);
               o.y = bf_hi(d) * dsilu_f(pre[nt][2 * h + 1]);
@@ -346,85 +378,107 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_bwd(TcArgs a) {
       }
     }
 
-    // ---- phase 2: per 16-row block: dx, m, dalpha, dbasis
-    for (int b = 0; b < 4; ++b) {
-      const bool active = 16 * b < rows;  // uniform across the CTA
-      if (active) {
-        float dzu[2][4];
-        load_dz(16 * b, dzu);
-        uint32_t ab[KT][4];  // alpha as the B operand of dbasis (tokens x bases)
+    // ---- phase 2: per 16-row block: dx, m = dz * x_shift, dalpha, dbasis
+    const int nb = (rows + 15) >> 4;  // uniform across the CTA
+#pragma unroll 1
+    for (int b = 0; b < nb; ++b) {
+      uint32_t ab[KT][4];  // alpha as the B operand of dbasis (tokens x bases)
 #pragma unroll
-        for (int kt = 0; kt < KT; ++kt)
-          ldsm_x4_t(smem_addr(a_s + (16 * b + lm_row(lane)) * L::ARB + (kt * 16 + lm_col(lane)) * 2), ab[kt]);
-        float dxa[2][4] = {};
-        float daa[2 * KT][4] = {};
+      for (int kt = 0; kt < KT; ++kt) ldsm_x4_t(a_s + (16 * b) * L::ARB + kt * 32 + a_lane, ab[kt]);
+      uint32_t dyu[4];     // dy of this block, packed bf16 pairs (no activation)
+      float dzu[2][4];     // fp32 dz of this block (SiLU)
+      if constexpr (ACT) {
+        load_dz32(16 * b, dzu);
+      } else {
+        ldsm_x4(dy_s + (16 * b) * kRowB + c_lane, dyu);
+      }
+      float dxa[2][4] = {};
+      float daa[2 * KT][4] = {};
 #pragma unroll
-        for (int s = 0; s < S; ++s) {
-          const int j = S - 1 - s;
-          if (want_dx) {
-            float w[2][4], dzs[2][4];
-            w_frag(16 * b + j, s, w);  // W at rows t + j
-            load_dz(16 * b + j, dzs);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) dxa[nt][e] = fmaf(w[nt][e], dzs[nt][e], dxa[nt][e]);
-          }
-          uint32_t xr[4];
-          ldsm_x4(smem_addr(x_s + (kHalo + 16 * b - j + lm_row(lane)) * kRowB + (ch_w + lm_col(lane)) * 2), xr);
-          uint32_t m[4];  // A operand (tokens x channels) of dalpha, rounded to bf16
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const int nt = r >> 1, h = r & 1;
-            m[r] = pack_bf16(dzu[nt][2 * h] * bf_lo(xr[r]), dzu[nt][2 * h + 1] * bf_hi(xr[r]));
-          }
-#pragma unroll
-          for (int kt = 0; kt < KT; ++kt) {
-            uint32_t bb[4];
-            ldsm_x4(smem_addr(basis_s + (s * KP + kt * 16 + (lane & 7) + (lane >> 4) * 8) * kRowB +
-                              (ch_w + ((lane >> 3) & 1) * 8) * 2),
-                    bb);
-            mma_bf16(daa[2 * kt], m, bb[0], bb[1]);
-            mma_bf16(daa[2 * kt + 1], m, bb[2], bb[3]);
-          }
-          uint32_t mt[4] = {movm_t(m[0]), movm_t(m[2]), movm_t(m[1]), movm_t(m[3])};
-#pragma unroll
-          for (int kt = 0; kt < KT; ++kt) {
-            mma_bf16(dba[s][2 * kt], mt, ab[kt][0], ab[kt][1]);
-            mma_bf16(dba[s][2 * kt + 1], mt, ab[kt][2], ab[kt][3]);
-          }
-        }
+      for (int s = 0; s < S; ++s) {
+        const int j = S - 1 - s;
         if (want_dx) {
+          float w[2][4];
+          w_frag(16 * b + j, s, w);  // W at rows t + j
+          if constexpr (ACT) {
+            float dzs[2][4];
+            load_dz32(16 * b + j, dzs);
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            const int64_t ch = ch_base + ch_w + nt * 8 + 2 * q;
+            for (int nt = 0; nt < 2; ++nt) {
+              ffma2(dxa[nt][0], dxa[nt][1], w[nt][0], w[nt][1], dzs[nt][0], dzs[nt][1]);
+              ffma2(dxa[nt][2], dxa[nt][3], w[nt][2], w[nt][3], dzs[nt][2], dzs[nt][3]);
+            }
+          } else {
+            uint32_t dys[4];
+            ldsm_x4(dy_s + (16 * b + j) * kRowB + c_lane, dys);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int64_t tok = r0 + 16 * b + g + 8 * h;
-              if (tok < r1 && ch < a.D)
-                *reinterpret_cast<uint32_t*>(a.dx + tok * a.D + ch) = pack_bf16(dxa[nt][2 * h], dxa[nt][2 * h + 1]);
+            for (int nt = 0; nt < 2; ++nt) {
+              ffma2(dxa[nt][0], dxa[nt][1], w[nt][0], w[nt][1], bf_lo(dys[2 * nt]), bf_hi(dys[2 * nt]));
+              ffma2(dxa[nt][2], dxa[nt][3], w[nt][2], w[nt][3], bf_lo(dys[2 * nt + 1]), bf_hi(dys[2 * nt + 1]));
             }
           }
         }
-        float* red = red_s + (red_buf * 8 + warp) * 16 * KP;
+        uint32_t xr[4];
+        ldsm_x4(x_s + (kHalo + 16 * b - j) * kRowB + c_lane, xr);
+        uint32_t m[4];  // A operand (tokens x channels) of dalpha, rounded to bf16
 #pragma unroll
-        for (int kn = 0; kn < 2 * KT; ++kn)
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-            *reinterpret_cast<float2*>(red + (g + 8 * h) * KP + kn * 8 + 2 * q) =
-                make_float2(daa[kn][2 * h], daa[kn][2 * h + 1]);
-        __syncthreads();
-        const float* rb = red_s + red_buf * 8 * 16 * KP;
-        for (int o = threadIdx.x; o < 16 * KP; o += kThreads) {
-          const int row = o / KP, k = o - row * KP;
-          float sum = 0.f;
-#pragma unroll
-          for (int w = 0; w < 8; ++w) sum += rb[w * 16 * KP + o];
-          const int64_t tok = r0 + 16 * b + row;
-          if (k < a.K && tok < r1) a.da_part[(slice * a.n_tokens + tok) * a.K + k] = sum;
+        for (int r = 0; r < 4; ++r) {
+          if constexpr (ACT) {
+            const int nt = r >> 1, h = r & 1;
+            m[r] = pack_bf16(dzu[nt][2 * h] * bf_lo(xr[r]), dzu[nt][2 * h + 1] * bf_hi(xr[r]));
+          } else {
+            m[r] = hmul2_bf16(dyu[r], xr[r]);
+          }
         }
-        red_buf ^= 1;
+#pragma unroll
+        for (int kt = 0; kt < KT; ++kt) {
+          if constexpr (BREG) {
+            mma_bf16(daa[2 * kt], m, bd[s][kt][0], bd[s][kt][1]);
+            mma_bf16(daa[2 * kt + 1], m, bd[s][kt][2], bd[s][kt][3]);
+          } else {
+            uint32_t bb[4];
+            ldsm_x4(basis_base + (s * KP + kt * 16) * kRowB + bn_lane, bb);
+            mma_bf16(daa[2 * kt], m, bb[0], bb[1]);
+            mma_bf16(daa[2 * kt + 1], m, bb[2], bb[3]);
+          }
+        }
+        uint32_t mt[4] = {movm_t(m[0]), movm_t(m[2]), movm_t(m[1]), movm_t(m[3])};
+#pragma unroll
+        for (int kt = 0; kt < KT; ++kt) {
+          mma_bf16(dba[s][2 * kt], mt, ab[kt][0], ab[kt][1]);
+          mma_bf16(dba[s][2 * kt + 1], mt, ab[kt][2], ab[kt][3]);
+        }
       }
+      if (want_dx) {
+        bf16* dx_row = a.dx + (r0 + 16 * b + g) * a.D + ch_base + ch_w + 2 * q;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (16 * b + g + 8 * h < rows) {
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+              if (ch_base + ch_w + nt * 8 < a.D)
+                *reinterpret_cast<uint32_t*>(dx_row + 8 * h * a.D + nt * 8) =
+                    pack_bf16(dxa[nt][2 * h], dxa[nt][2 * h + 1]);
+          }
+        }
+      }
+      float* red = red_s + (red_buf * 8 + warp) * 16 * KP;
+#pragma unroll
+      for (int kn = 0; kn < 2 * KT; ++kn)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          *reinterpret_cast<float2*>(red + (g + 8 * h) * KP + kn * 8 + 2 * q) =
+              make_float2(daa[kn][2 * h], daa[kn][2 * h + 1]);
+      __syncthreads();
+      const float* rb = red_s + red_buf * 8 * 16 * KP;
+      for (int o = threadIdx.x; o < 16 * KP; o += kThreads) {
+        const int row = o / KP, k = o - row * KP;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sum += rb[w * 16 * KP + o];
+        if (k < a.K && 16 * b + row < rows) a.da_part[(slice * a.n_tokens + r0 + 16 * b + row) * a.K + k] = sum;
+      }
+      red_buf ^= 1;
     }
     __syncthreads();
   }
@@ -509,7 +563,7 @@ int launch(Kern kern, bool (&configured)[64], dim3 grid, int smem, cudaStream_t 
 template <int KT, int S, bool ACT>
 int fwd_inst(const moc_problem& p, TcArgs& args, cudaStream_t st) {
   using L = Layout<KT, S, ACT, false>;
-  const Plan pl = make_plan(p, 3);
+  const Plan pl = make_plan(p, L::min_blocks);
   args.rm = pl.rm;
   args.items_per_group = pl.ipg;
   if (pl.rm.n_items() == 0) return MOC_OK;
@@ -521,7 +575,8 @@ int fwd_inst(const moc_problem& p, TcArgs& args, cudaStream_t st) {
 template <int KT, int S, bool ACT>
 int bwd_inst(const moc_problem& p, TcArgs& args, void* dalpha, void* dbasis, cudaStream_t st) {
   using L = Layout<KT, S, ACT, true>;
-  const Plan pl = make_plan(p, 1);
+  static_assert(L::min_blocks == ((L::BREG && !ACT && KT == 1) ? 2 : 1), "bwd_min_blocks() mirrors Layout::min_blocks");
+  const Plan pl = make_plan(p, L::min_blocks);
   args.rm = pl.rm;
   args.items_per_group = pl.ipg;
   const int64_t nk = p.n_tokens * p.n_bases;
@@ -565,8 +620,16 @@ struct BwdRun {
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
+// Resident backward CTAs per SM for problem p (Layout::min_blocks of the instantiation
+// dispatch() selects); the workspace size and the launch must agree on it.
+int bwd_min_blocks(const moc_problem& p) {
+  const int kt = p.n_bases <= 16 ? 1 : 2;
+  const bool breg = kt * p.kernel_size <= 4;
+  return (breg && p.activation == 0 && kt == 1) ? 2 : 1;
+}
+
 void ws_split(const moc_problem& p, int64_t& slices, int64_t& groups, size_t& da_bytes, size_t& db_bytes) {
-  const Plan pl = make_plan(p, 1);
+  const Plan pl = make_plan(p, bwd_min_blocks(p));
   slices = pl.slices;
   groups = pl.groups;
   da_bytes = align_up(static_cast<size_t>(slices * p.n_tokens * p.n_bases) * sizeof(float), 256);
