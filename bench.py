@@ -74,8 +74,26 @@ def measured_peaks() -> dict:
 
 # ----------------------------------------------------------------------------- clocks
 
+_SAMPLER_SRC = r"""
+import sys, time, pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByPciBusId(sys.argv[1].encode())
+out = open(sys.argv[2], "w", buffering=1)
+out.write("max %d\n" % pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+while True:
+    mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+    try:
+        reasons = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+    except Exception:
+        reasons = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+    out.write("%.6f %d %d\n" % (time.time(), mhz, reasons))
+    time.sleep(0.001)
+"""
+
+
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML every ~2 ms in a thread."""
+    """Samples the SM clock and clock-event (throttle) reasons of one GPU through NVML
+    every ~1 ms in a child process (free of this process's GIL), tagged with wall time."""
 
     REASONS = {
         "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
@@ -83,54 +101,48 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80,
     }
 
-    def __init__(self, device: torch.device) -> None:
-        self.samples: list[tuple[float, int, int]] = []
-        self.max_mhz = None
-        self._stop = threading.Event()
-        self._thread = None
-        try:
-            import pynvml
-            pynvml.nvmlInit()
-            self._nvml = pynvml
-            props = torch.cuda.get_device_properties(device)
-            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
-            self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
-        except Exception:  # noqa: BLE001
-            self._nvml = None
+    def __init__(self, device: torch.device, out_dir: str) -> None:
+        import subprocess
 
-    def _run(self) -> None:
-        n = self._nvml
-        while not self._stop.is_set():
-            try:
-                mhz = n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)
-                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                self.samples.append((time.perf_counter(), mhz, reasons))
-            except Exception:  # noqa: BLE001
-                pass
-            time.sleep(0.002)
-
-    def start(self) -> None:
-        if self._nvml is not None:
-            self._thread = threading.Thread(target=self._run, daemon=True)
-            self._thread.start()
+        props = torch.cuda.get_device_properties(device)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        self.path = os.path.join(out_dir, f"clocks_{os.getpid()}.txt")
+        self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_SRC, bus, self.path],
+                                     stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        deadline = time.time() + 60
+        while time.time() < deadline and self.proc.poll() is None:  # wait for the first sample
+            if os.path.exists(self.path) and os.path.getsize(self.path) > 20:
+                break
+            time.sleep(0.05)
 
     def stop(self) -> None:
-        self._stop.set()
-        if self._thread is not None:
-            self._thread.join()
+        if self.proc.poll() is None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
 
     def summary(self, t0: float, t1: float) -> dict:
-        if self._nvml is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
-        inside = [s for s in self.samples if t0 <= s[0] <= t1] or self.samples[-3:]
-        mhz = [s[1] for s in inside]
+        self.stop()
+        max_mhz, samples = None, []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = line.split()
+                    if parts and parts[0] == "max":
+                        max_mhz = int(parts[1])
+                    elif len(parts) == 3:
+                        samples.append((float(parts[0]), int(parts[1]), int(parts[2])))
+            os.remove(self.path)
+        except OSError:
+            pass
+        if not samples:
+            return {"sm_mhz": None, "sm_max_mhz": max_mhz, "reasons": ["no NVML samples"], "samples": 0}
+        inside = [s for s in samples if t0 <= s[0] <= t1] or [min(samples, key=lambda s: abs(s[0] - t1))]
         mask = 0
         for s in inside:
             mask |= s[2]
         reasons = [name for name, bit in self.REASONS.items() if mask & bit and name != "gpu_idle"]
-        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(inside)}
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": max_mhz, "reasons": reasons,
+                "samples": len(inside)}
 
 
 # ----------------------------------------------------------------------------- workload
@@ -320,12 +332,11 @@ def main() -> None:
 
     for _ in range(args.warmup):
         graph_step()
-    sampler = ClockSampler(device)
-    sampler.start()
+    sampler = ClockSampler(device, os.environ.get("TMPDIR", "/tmp"))
     barrier(world)
-    t_wall0 = time.perf_counter()
+    t_wall0 = time.time()
     ms_step = time_region(graph_step, args.steps, stream)
-    t_wall1 = time.perf_counter()
+    t_wall1 = time.time()
     barrier(world)
     ms_step = max_over_ranks(ms_step, world)
     clocks = sampler.summary(t_wall0, t_wall1)

@@ -84,6 +84,18 @@ const char* moc_last_cuda_error(void);
  * streams); lets a caller count launches over a region of work. */
 uint64_t moc_launch_count(void);
 
+/* Device status word of the TMA-staged kernels, OR of MOC_STATUS_* bits recorded since
+ * the last clear (synchronous: reads device memory).  A staging wait that runs out of
+ * its poll budget records MOC_STATUS_WAIT_TIMEOUT and the kernel returns without
+ * writing its outputs instead of hanging. */
+#define MOC_STATUS_WAIT_TIMEOUT 1
+int moc_device_status(int* status, int clear);
+
+/* Diagnostic: launches one thread that waits, with `poll_limit` polls, on an mbarrier
+ * nothing arrives on; it records MOC_STATUS_WAIT_TIMEOUT through the same path as the
+ * staging kernels.  Used by the tests of the bounded-wait path. */
+int moc_wait_timeout_probe(uint32_t poll_limit, void* stream);
+
 /* Kernel family selection for every later call in this process: MOC_PATH_AUTO (tensor
  * cores for the bf16 shapes they support, the default) or MOC_PATH_GENERIC (the fp32
  * CUDA-core kernels for every shape).  Both compute the complete result; the switch

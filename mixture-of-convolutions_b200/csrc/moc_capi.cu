@@ -1,12 +1,16 @@
 // extern "C" entry points declared in include/moc_b200.h: argument checks, then
 // dispatch to the tensor-core kernels (bf16 shapes they support) or the generic
 // CUDA-core kernels.  No entry point allocates memory or synchronises the host.
+#include <cudaTypedefs.h>
+
 #include <atomic>
 #include <cstdlib>
+#include <mutex>
 #include <string>
 
 #include "moc_common.cuh"
 #include "moc_internal.h"
+#include "moc_tma.cuh"
 
 namespace moc {
 
@@ -43,6 +47,36 @@ static int check_problem(const moc_problem* p) {
   return MOC_OK;
 }
 
+int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                      uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (encode == nullptr) {
+    g_last_cuda_error = "cuTensorMapEncodeTiled entry point unavailable";
+    return MOC_ERR_CUDA;
+  }
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    g_last_cuda_error = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r));
+    return MOC_ERR_CUDA;
+  }
+  return MOC_OK;
+}
+
 static bool use_tc(const moc_problem& p) { return g_kernel_path == 0 && tc_conv_supported(p); }
 
 }  // namespace moc
@@ -69,6 +103,20 @@ const char* moc_error_string(int code) {
 const char* moc_last_cuda_error(void) { return g_last_cuda_error.c_str(); }
 
 uint64_t moc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int moc_device_status(int* status, int clear) {
+  if (status == nullptr) return MOC_ERR_INVALID_ARGUMENT;
+  int r = 0, c = 0;
+  int rc = router_status(&r, clear != 0);
+  if (rc == MOC_OK) rc = conv_status(&c, clear != 0);
+  if (rc != MOC_OK) return rc;
+  *status = r | c;
+  return MOC_OK;
+}
+
+int moc_wait_timeout_probe(uint32_t poll_limit, void* stream) {
+  return wait_timeout_probe(poll_limit, static_cast<cudaStream_t>(stream));
+}
 
 // Selects the kernel family: 0 = automatic (tensor cores where supported),
 // 1 = generic CUDA-core kernels for every shape.  Both compute the full result.

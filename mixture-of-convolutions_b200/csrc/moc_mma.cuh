@@ -40,6 +40,15 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// d = a * b  (m16n8k16, bf16 x bf16 -> fp32, zero accumulator)
+__device__ __forceinline__ void mma_bf16_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
 // Transpose one 8x8 b16 fragment held one register per thread.
 __device__ __forceinline__ uint32_t movm_t(uint32_t v) {
   uint32_t r;
@@ -58,12 +67,9 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 // (d0, d1) += (a0, a1) * (b0, b1) as one packed fp32x2 FMA (sm_100 FFMA2).
 __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  uint64_t d, a, b;
-  asm("mov.b64 %0, {%1,%2};" : "=l"(a) : "f"(a0), "f"(a1));
-  asm("mov.b64 %0, {%1,%2};" : "=l"(b) : "f"(b0), "f"(b1));
-  asm("mov.b64 %0, {%1,%2};" : "=l"(d) : "f"(d0), "f"(d1));
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
-  asm("mov.b64 {%0,%1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+  const float2 r = __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), make_float2(d0, d1));
+  d0 = r.x;
+  d1 = r.y;
 }
 
 // Elementwise bf16x2 product rounded to bf16 (nearest even).  For bf16 inputs the exact

@@ -18,6 +18,7 @@
 #include "moc_common.cuh"
 #include "moc_internal.h"
 #include "moc_mma.cuh"
+#include "moc_tma.cuh"
 
 namespace moc {
 namespace {
@@ -33,75 +34,92 @@ __device__ __forceinline__ int lm_col(int lane) { return (lane >> 4) * 8; }
 
 // ------------------------------------------------------------------ forward
 
+__device__ int g_router_status;  // kStatus* bits of bounded waits that ran out
+
 template <int KT>
 struct FwdLayout {
   static constexpr int KP = KT * 16;
-  static constexpr int z_bytes = kFwdRows * kRowB;
-  static constexpr int w_bytes = KP * kRowB;
-  static constexpr int stage_bytes = z_bytes + w_bytes;
-  static constexpr int total = kFwdStages * stage_bytes;
+  static constexpr int zbox = kFwdRows * 128;  // one 64-token x 64-column box, 128 B rows
+  static constexpr int wbox = KP * 128;        // one KP-base x 64-column box
+  static constexpr int stage_bytes = 2 * zbox + 2 * wbox;  // 128 columns of z and W
+  static constexpr int tx_bytes = stage_bytes;
+  static constexpr int total = kFwdStages * stage_bytes + 1024 + 64;  // + alignment slack + mbarriers
 };
 
+// TMA-staged forward: thread 0 keeps kFwdStages chunks of 128 z columns (two 64-column
+// boxes of z and of W, 128-byte swizzled) in flight on per-stage mbarriers.
 template <int KT>
-__global__ void __launch_bounds__(128) k_router_fwd_tc(const bf16* __restrict__ z, const bf16* __restrict__ w,
+__global__ void __launch_bounds__(128) k_router_fwd_tc(const __grid_constant__ CUtensorMap zmap,
+                                                       const __grid_constant__ CUtensorMap wmap,
                                                        bf16* __restrict__ alpha, int64_t N, int64_t Dz, int K,
                                                        int act) {
   using L = FwdLayout<KT>;
-  extern __shared__ __align__(128) char smem[];
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_addr(smem);
+  const uint32_t bar0 = sbase + kFwdStages * L::stage_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kFwdRows;
   const int n_chunks = static_cast<int>((Dz + kZC - 1) / kZC);
 
-  auto load_chunk = [&](int c) {
-    char* st = smem + (c % kFwdStages) * L::stage_bytes;
-    const int64_t col0 = static_cast<int64_t>(c) * kZC;
-    for (int idx = threadIdx.x; idx < (kFwdRows + L::KP) * 16; idx += 128) {
-      const int row = idx >> 4, chunk = idx & 15;
-      const int64_t col = col0 + chunk * 8;
-      if (row < kFwdRows) {
-        const int64_t tok = t0 + row;
-        const bool ok = tok < N && col < Dz;
-        cp_async16(smem_addr(st + row * kRowB + chunk * 16), ok ? z + tok * Dz + col : z, ok ? 16u : 0u);
-      } else {
-        const int k = row - kFwdRows;
-        const bool ok = k < K && col < Dz;
-        cp_async16(smem_addr(st + L::z_bytes + k * kRowB + chunk * 16), ok ? w + k * Dz + col : w,
-                   ok ? 16u : 0u);
-      }
-    }
+  auto issue = [&](int c) {
+    const int st = c % kFwdStages;
+    const uint32_t dst = sbase + st * L::stage_bytes;
+    const uint32_t bar = bar0 + 8 * st;
+    mbar_expect_tx(bar, L::tx_bytes);
+    tma_load_2d(dst, &zmap, c * kZC, static_cast<int>(t0), bar);
+    tma_load_2d(dst + L::zbox, &zmap, c * kZC + 64, static_cast<int>(t0), bar);
+    tma_load_2d(dst + 2 * L::zbox, &wmap, c * kZC, 0, bar);
+    tma_load_2d(dst + 2 * L::zbox + L::wbox, &wmap, c * kZC + 64, 0, bar);
   };
 
-#pragma unroll
-  for (int c = 0; c < kFwdStages - 1; ++c) {
-    if (c < n_chunks) load_chunk(c);
-    cp_async_commit();
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&zmap);
+    tma_prefetch_desc(&wmap);
+    for (int st = 0; st < kFwdStages; ++st) mbar_init(bar0 + 8 * st, 1);
+    fence_mbar_init();
   }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int c = 0; c < kFwdStages && c < n_chunks; ++c) issue(c);
+
   float acc[2 * KT][4] = {};
   for (int c = 0; c < n_chunks; ++c) {
-    cp_async_wait<kFwdStages - 2>();
-    __syncthreads();
-    if (c + kFwdStages - 1 < n_chunks) load_chunk(c + kFwdStages - 1);
-    cp_async_commit();
-    const char* st = smem + (c % kFwdStages) * L::stage_bytes;
-    const char* z_s = st;
-    const char* w_s = st + L::z_bytes;
+    const int st = c % kFwdStages;
+    const bool ok = mbar_wait(bar0 + 8 * st, (c / kFwdStages) & 1);
+    if (__syncthreads_or(!ok)) {
+      // a copy did not land in time: record it, wait (bounded) for what is in flight, stop
+      if (threadIdx.x == 0) {
+        atomicOr(&g_router_status, kStatusWaitTimeout);
+        for (int cc = c; cc < n_chunks && cc < c + kFwdStages; ++cc)
+          mbar_wait(bar0 + 8 * (cc % kFwdStages), (cc / kFwdStages) & 1);
+      }
+      return;
+    }
+    const uint32_t zs = sbase + st * L::stage_bytes;
+    const uint32_t ws = zs + 2 * L::zbox;
 #pragma unroll
     for (int kk = 0; kk < kZC / 16; ++kk) {
       uint32_t af[4];
-      ldsm_x4(smem_addr(z_s + (warp * 16 + lm_row(lane)) * kRowB + (kk * 16 + lm_col(lane)) * 2), af);
+      {
+        const int row = warp * 16 + lm_row(lane);
+        const int c16 = kk * 2 + (lane >> 4);
+        ldsm_x4(zs + (c16 >> 3) * L::zbox + sw128(row, c16 & 7), af);
+      }
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt) {
-        uint32_t bb[4];  // (k 0-7 | 8-15) x (dz 0-7 | 8-15) of this 16-base group
-        ldsm_x4(smem_addr(w_s + (kt * 16 + (lane & 7) + (lane >> 4) * 8) * kRowB +
-                          (kk * 16 + ((lane >> 3) & 1) * 8) * 2),
-                bb);
+        uint32_t bb[4];  // (k 0-7 | 8-15) x (z columns 0-7 | 8-15) of this 16-base group
+        const int k = kt * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int c16 = kk * 2 + ((lane >> 3) & 1);
+        ldsm_x4(ws + (c16 >> 3) * L::wbox + sw128(k, c16 & 7), bb);
         mma_bf16(acc[2 * kt], af, bb[0], bb[1]);
         mma_bf16(acc[2 * kt + 1], af, bb[2], bb[3]);
       }
     }
+    __syncthreads();  // every warp is done with this stage before it is refilled
+    if (threadIdx.x == 0 && c + kFwdStages < n_chunks) issue(c + kFwdStages);
   }
-  cp_async_wait<0>();
 
   // acc[kn][2h + e] = logit(token warp*16 + g + 8h, base 8kn + 2q + e); the 4 lanes of a
   // quad hold one token row.
@@ -144,6 +162,16 @@ __global__ void __launch_bounds__(128) k_router_fwd_tc(const bf16* __restrict__ 
       }
     }
   }
+}
+
+// Diagnostic: waits on an mbarrier that nothing arrives on, with `limit` polls, and
+// records the timeout exactly like the staging kernels do.
+__global__ void k_wait_timeout_probe(uint32_t limit) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = smem_addr(&bar);
+  mbar_init(b, 1);
+  fence_mbar_init();
+  if (!mbar_wait(b, 0, limit)) atomicOr(&g_router_status, kStatusWaitTimeout);
 }
 
 // ------------------------------------------------------------------ backward
@@ -302,7 +330,8 @@ __global__ void k_sum_groups(const float* __restrict__ part, int64_t groups, int
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float s = 0.f;
-    for (int64_t g = 0; g < groups; ++g) s += part[g * n + i];
+#pragma unroll 8
+    for (int64_t g = 0; g < groups; ++g) s += __ldg(part + g * n + i);
     st_any(out, dtype, i, s);
   }
 }
@@ -341,8 +370,15 @@ int fwd_kt(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, 
   static bool configured[64] = {};
   int rc = set_smem(reinterpret_cast<const void*>(k_router_fwd_tc<KT>), configured, FwdLayout<KT>::total);
   if (rc != MOC_OK) return rc;
+  CUtensorMap zmap, wmap;
+  rc = make_tmap_bf16_2d(&zmap, z, static_cast<uint64_t>(Dz), static_cast<uint64_t>(N),
+                         static_cast<uint64_t>(Dz) * 2, 64, kFwdRows);
+  if (rc != MOC_OK) return rc;
+  rc = make_tmap_bf16_2d(&wmap, w, static_cast<uint64_t>(Dz), static_cast<uint64_t>(K), static_cast<uint64_t>(Dz) * 2,
+                         64, KT * 16);
+  if (rc != MOC_OK) return rc;
   k_router_fwd_tc<KT><<<static_cast<unsigned>(ceil_div(N, kFwdRows)), 128, FwdLayout<KT>::total, st>>>(
-      static_cast<const bf16*>(z), static_cast<const bf16*>(w), static_cast<bf16*>(alpha), N, Dz, K, act);
+      zmap, wmap, static_cast<bf16*>(alpha), N, Dz, K, act);
   note_launch();
   return note_cuda(cudaGetLastError());
 }
@@ -404,6 +440,25 @@ int tc_router_backward(int64_t N, int64_t Dz, int K, int act, const void* z, con
   bwd_plan(N, Dz, slices, groups, tpg);
   a.tiles_per_group = tpg;
   return K <= 16 ? bwd_kt<1>(a, slices, groups, dw, st) : bwd_kt<2>(a, slices, groups, dw, st);
+}
+
+int router_status(int* out, bool clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_router_status, sizeof(int));
+  if (e != cudaSuccess) return note_cuda(e);
+  if (clear && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_router_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return note_cuda(e);
+  }
+  *out = v;
+  return MOC_OK;
+}
+
+int wait_timeout_probe(uint32_t limit, cudaStream_t st) {
+  k_wait_timeout_probe<<<1, 1, 0, st>>>(limit);
+  note_launch();
+  return note_cuda(cudaGetLastError());
 }
 
 }  // namespace moc

@@ -1,17 +1,19 @@
-// Tensor-core MoC convolution for bf16 x / alpha / basis (sm_100a, mma.sync bf16 -> fp32).
+// Tensor-core MoC convolution for bf16 x / alpha / basis (sm_100a).
 //
 // The three K-contractions of the operator are small GEMMs per tile:
 //   W[t, s, ch]   = sum_k alpha[t, k] basis[k, s, ch]             (forward, dx, SiLU pre)
 //   dalpha[t, k]  = sum_{s,ch} m[t, s, ch] basis[k, s, ch]        (m = dz * x shifted)
 //   dbasis[k,s,ch]= sum_t alpha[t, k] m[t, s, ch]
-// They run on the tensor cores with fp32 accumulation; the shifts, SiLU and the dz*x
+// They run on the tensor cores (mma.sync bf16 -> fp32); the shifts, SiLU and the dz*x
 // products run on the CUDA cores in registers, so the per-token kernel W and the product
 // m never touch memory.  Rounding points follow the reference's bf16 mode
 // (moc/kernels.py:92-95, 125-130, 390-408): alpha, basis and m enter the dots as bf16.
 //
 // Work decomposition: a CTA owns a 128-channel slice and a contiguous range of 64-token
 // work items (fixed-length tiles or the varlen chunks of chunk_indices); 8 warps each own
-// 16 channels.  Tiles are staged in shared memory with cp.async, double buffered.
+// 16 channels.  Tiles are staged by TMA (two 64-channel 128B-swizzled boxes of x and dy,
+// one dense box of alpha per stage, double buffered on mbarriers, issued by one thread);
+// rows that belong to a neighbouring sequence are zeroed in shared memory after landing.
 //   forward : y = [silu](sum_s W_s * x_shift_s)                       one pass
 //   backward: dz (SiLU pre recomputed on chip), dx, per-slice dalpha partials and per-CTA
 //             dbasis partials in one pass over x, dy, alpha; a second small kernel adds the
@@ -21,21 +23,27 @@
 #include "moc_common.cuh"
 #include "moc_internal.h"
 #include "moc_mma.cuh"
+#include "moc_tma.cuh"
 
 namespace moc {
+
+__device__ int g_conv_status;  // kStatus* bits of bounded waits that ran out
+
 namespace {
 
-constexpr int kTile = 64;                  // token rows per work item
-constexpr int kBD = 128;                   // channels per CTA
-constexpr int kThreads = 256;              // 8 warps x 16 channels
-constexpr int kRowB = (kBD + 8) * 2;       // bf16 channel row in smem: 272 B (16 B pad: conflict-free ldmatrix)
-constexpr int kDzRowB = (kBD + 8) * 4;     // fp32 dz row: 544 B
-constexpr int kHalo = 8;                   // past-halo rows kept before each tile (S - 1 <= 7)
-constexpr int kFut = 16;                   // future rows kept after each tile (S - 1 <= 7, one 16-row block)
+constexpr int kTile = 64;              // token rows per work item
+constexpr int kBD = 128;               // channels per CTA (two 64-channel TMA boxes)
+constexpr int kThreads = 256;          // 8 warps x 16 channels
+constexpr int kRowB = (kBD + 8) * 2;   // basis row in smem: 272 B (16 B pad: conflict-free ldmatrix)
+constexpr int kDzRowB = (kBD + 8) * 4; // fp32 dz row: 544 B
+constexpr int kHalo = 8;               // past-halo rows kept before each tile (S - 1 <= 7)
+constexpr int kFut = 16;               // future rows kept after each tile (S - 1 <= 7, one 16-row block)
+
+constexpr int align1k(int v) { return (v + 1023) / 1024 * 1024; }
 
 template <int KT, int S, bool ACT, bool BWD>
 struct Layout {
-  static constexpr int KP = KT * 16;                                   // bases padded to the MMA K
+  static constexpr int KP = KT * 16;  // bases padded to the MMA K
   // basis fragments live in registers when they fit (<= 4 (tap, 16-base) groups)
   static constexpr bool BREG = KT * S <= 4;
   static constexpr int XR = kHalo + kTile + ((BWD && ACT) ? kFut : 0);  // x rows per stage
@@ -43,30 +51,30 @@ struct Layout {
   // with SiLU the pre-activation of those rows is one more 16-row MMA block.
   static constexpr int FR = BWD ? (ACT ? kTile + kFut : kTile + 8) : 0;
   static constexpr int AR = BWD ? (ACT ? kTile + kFut : kTile + 8) : kTile;
-  static constexpr int ARB = (KP + 8) * 2;                             // alpha row bytes (48 / 80)
-  static constexpr int basis_bytes = S * KP * kRowB;
-  static constexpr int x_bytes = XR * kRowB;
-  static constexpr int dy_bytes = FR * kRowB;
-  static constexpr int a_bytes = AR * ARB;
+  static constexpr int ARB = KP * 2;  // dense alpha rows
+  static constexpr int xbox = XR * 128;
+  static constexpr int dybox = FR * 128;
+  static constexpr int x_bytes = 2 * xbox;
+  static constexpr int dy_bytes = 2 * dybox;
+  static constexpr int a_bytes = align1k(AR * ARB);
   static constexpr int stage_bytes = x_bytes + dy_bytes + a_bytes;
-  static constexpr int dz_bytes = (BWD && ACT) ? FR * kDzRowB : 0;
+  static constexpr int tx_bytes = x_bytes + dy_bytes + AR * ARB;
+  static constexpr int basis_bytes = S * KP * kRowB;
   static constexpr int red_bytes = BWD ? 2 * 8 * 16 * KP * 4 : 0;
   // with register-resident basis fragments the basis staging area is reused for the
   // dalpha reduction buffer once the fragments are loaded
-  static constexpr int head_bytes = (BWD && BREG) ? (basis_bytes > red_bytes ? basis_bytes : red_bytes)
-                                                  : basis_bytes + red_bytes;
-  static constexpr int total = head_bytes + 2 * stage_bytes + dz_bytes;
-  static constexpr int min_blocks = BWD ? ((BREG && !ACT && KT == 1) ? 2 : 1) : (KT == 1 ? 3 : 2);
+  static constexpr int head_bytes =
+      align1k((BWD && BREG) ? (basis_bytes > red_bytes ? basis_bytes : red_bytes) : basis_bytes + red_bytes);
+  static constexpr int dz_bytes = (BWD && ACT) ? FR * kDzRowB : 0;
+  static constexpr int total = 1024 + 2 * stage_bytes + head_bytes + dz_bytes + 64;
+  static constexpr int min_blocks = BWD ? ((BREG && !ACT && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 3 : 2);
 };
 
 struct TcArgs {
   RowMap rm;
   int64_t D;
   int K;
-  const bf16* x;
-  const bf16* alpha;
   const bf16* basis;
-  const bf16* dy;
   bf16* out;
   bf16* dx;
   float* da_part;  // [n_slices][n_tokens][K]
@@ -75,9 +83,30 @@ struct TcArgs {
   int64_t n_tokens;
 };
 
-// ------------------------------------------------------------------ staging
+// lane -> row / column offsets of the four 8x8 matrices of an ldmatrix.x4 covering a
+// 16(rows) x 16(cols) block: matrix i = lane/8 holds rows (i&1)*8.. and cols (i>>1)*8..
+__device__ __forceinline__ int lm_row(int lane) { return (lane & 7) + ((lane >> 3) & 1) * 8; }
+__device__ __forceinline__ int lm_col(int lane) { return (lane >> 4) * 8; }
 
-template <class L, bool BWD, bool ACT>
+// Shared-memory carve-up, common to both kernels.
+template <class L>
+struct Smem {
+  uint32_t stages;  // 2 stages, 1024-byte aligned
+  char* stages_p;
+  char* head;       // basis staging / dalpha reduction
+  char* dz;         // fp32 dz (SiLU backward)
+  uint32_t bar;     // 2 mbarriers
+  __device__ explicit Smem(char* raw) {
+    char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    stages_p = base;
+    stages = smem_addr(base);
+    head = base + 2 * L::stage_bytes;
+    dz = head + L::head_bytes;
+    bar = smem_addr(dz + L::dz_bytes);
+  }
+};
+
+template <class L, bool BWD>
 __device__ __forceinline__ void load_basis(const TcArgs& a, char* basis_s, int64_t ch_base, int S) {
   constexpr int KP = L::KP;
   for (int idx = threadIdx.x; idx < S * KP * 16; idx += kThreads) {
@@ -90,55 +119,47 @@ __device__ __forceinline__ void load_basis(const TcArgs& a, char* basis_s, int64
   }
 }
 
-template <class L, bool BWD, bool ACT>
-__device__ __forceinline__ void load_tile(const TcArgs& a, char* stage, int64_t ss, int64_t se, int64_t r0,
-                                          int64_t r1, int64_t ch_base) {
-  char* x_s = stage;
-  char* dy_s = stage + L::x_bytes;
-  char* a_s = stage + L::x_bytes + L::dy_bytes;
-  const int64_t x_hi = (BWD && ACT) ? se : r1;
-  for (int idx = threadIdx.x; idx < L::XR * 16; idx += kThreads) {
-    const int row = idx >> 4, chunk = idx & 15;
-    const int64_t tok = r0 - kHalo + row;
-    const int64_t ch = ch_base + chunk * 8;
-    const bool ok = tok >= ss && tok < x_hi && ch < a.D;
-    const bf16* src = ok ? a.x + tok * a.D + ch : a.x;
-    cp_async16(smem_addr(x_s + row * kRowB + chunk * 16), src, ok ? 16u : 0u);
-  }
+// Thread 0: stage `stage` <- tile starting at token r0 (x from r0 - kHalo), channel slice ch_base.
+template <class L, bool BWD>
+__device__ __forceinline__ void issue_tile(const CUtensorMap* xm, const CUtensorMap* dym, const CUtensorMap* am,
+                                           uint32_t stage, uint32_t bar, int64_t r0, int64_t ch_base) {
+  fence_proxy_async();
+  mbar_expect_tx(bar, L::tx_bytes);
+  const int c0 = static_cast<int>(ch_base);
+  const int row = static_cast<int>(r0);
+  tma_load_2d(stage, xm, c0, row - kHalo, bar);
+  tma_load_2d(stage + L::xbox, xm, c0 + 64, row - kHalo, bar);
   if constexpr (BWD) {
-    for (int idx = threadIdx.x; idx < L::FR * 16; idx += kThreads) {
-      const int row = idx >> 4, chunk = idx & 15;
-      const int64_t tok = r0 + row;
-      const int64_t ch = ch_base + chunk * 8;
-      const bool ok = tok < se && ch < a.D;
-      const bf16* src = ok ? a.dy + tok * a.D + ch : a.dy;
-      cp_async16(smem_addr(dy_s + row * kRowB + chunk * 16), src, ok ? 16u : 0u);
-    }
+    tma_load_2d(stage + L::x_bytes, dym, c0, row, bar);
+    tma_load_2d(stage + L::x_bytes + L::dybox, dym, c0 + 64, row, bar);
   }
-  constexpr int kChunks = L::KP / 8;
-  const int64_t a_hi = BWD ? se : r1;
-  for (int idx = threadIdx.x; idx < L::AR * kChunks; idx += kThreads) {
-    const int row = idx / kChunks, chunk = idx - row * kChunks;
-    const int64_t tok = r0 + row;
-    const bool ok = tok < a_hi && chunk * 8 < a.K;
-    const bf16* src = ok ? a.alpha + tok * a.K + chunk * 8 : a.alpha;
-    cp_async16(smem_addr(a_s + row * L::ARB + chunk * 16), src, ok ? 16u : 0u);
-  }
+  tma_load_2d(stage + L::x_bytes + L::dy_bytes, am, 0, row, bar);
 }
 
-// lane -> row / column offsets of the four 8x8 matrices of an ldmatrix.x4 covering a
-// 16(rows) x 16(cols) block: matrix i = lane/8 holds rows (i&1)*8.. and cols (i>>1)*8..
-__device__ __forceinline__ int lm_row(int lane) { return (lane & 7) + ((lane >> 3) & 1) * 8; }
-__device__ __forceinline__ int lm_col(int lane) { return (lane >> 4) * 8; }
+// Zeroes rows [0, zx) of the x tile and rows [zdy, FR) of the dy tile (whole 128-byte
+// rows of both boxes): taps and gradients must not see a neighbouring sequence.
+template <class L>
+__device__ __forceinline__ void zero_rows(char* stage, int zx, int zdy) {
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  for (int idx = threadIdx.x; idx < zx * 16; idx += kThreads) {
+    const int row = idx >> 4, part = idx & 15;
+    *reinterpret_cast<uint4*>(stage + (part >> 3) * L::xbox + row * 128 + (part & 7) * 16) = z;
+  }
+  const int ndy = L::FR - zdy;
+  for (int idx = threadIdx.x; idx < ndy * 16; idx += kThreads) {
+    const int row = zdy + (idx >> 4), part = idx & 15;
+    *reinterpret_cast<uint4*>(stage + L::x_bytes + (part >> 3) * L::dybox + row * 128 + (part & 7) * 16) = z;
+  }
+}
 
 // ------------------------------------------------------------------ forward
 
 template <int KT, int S, bool ACT>
-__global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_blocks)) k_tc_fwd(TcArgs a) {
+__global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_blocks))
+    k_tc_fwd(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap amap, TcArgs a) {
   using L = Layout<KT, S, ACT, false>;
-  extern __shared__ __align__(128) char smem[];
-  char* basis_s = smem;
-  char* stages = smem + L::head_bytes;
+  extern __shared__ __align__(1024) char smem_raw[];
+  const Smem<L> sm(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int64_t ch_base = static_cast<int64_t>(blockIdx.x) * kBD;
@@ -147,43 +168,72 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
   const int64_t i1 = i0 + a.items_per_group < n_items ? i0 + a.items_per_group : n_items;
   if (i0 >= i1) return;
 
-  load_basis<L, false, ACT>(a, basis_s, ch_base, S);
-  {
-    int64_t ss, se, r0, r1;
-    if (a.rm.item(i0, ss, se, r0, r1)) load_tile<L, false, ACT>(a, stages, ss, se, r0, r1, ch_base);
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&xmap);
+    tma_prefetch_desc(&amap);
+    mbar_init(sm.bar, 1);
+    mbar_init(sm.bar + 8, 1);
+    fence_mbar_init();
   }
+  load_basis<L, false>(a, sm.head, ch_base, S);
   cp_async_commit();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t ss, se, r0, r1;
+    if (a.rm.item(i0, ss, se, r0, r1))
+      issue_tile<L, false>(&xmap, nullptr, &amap, sm.stages, sm.bar, r0, ch_base);
+    else
+      mbar_arrive(sm.bar);
+  }
 
-  // per-lane shared-memory offsets of the ldmatrix row addresses
-  const uint32_t a_lane = static_cast<uint32_t>(lm_row(lane) * L::ARB + lm_col(lane) * 2);
-  const uint32_t x_lane = static_cast<uint32_t>(lm_row(lane) * kRowB + (warp * 16 + lm_col(lane)) * 2);
+  // per-lane constants of the swizzled ldmatrix addresses: this warp's 16 channels are
+  // 16-byte chunks 2*(warp&3) + {0,1} of box warp>>2
+  const uint32_t x_box = static_cast<uint32_t>((warp >> 2) * L::xbox);
+  const int x_chunk = 2 * (warp & 3) + (lane >> 4);
+  const int lrow = lm_row(lane);
+  const uint32_t a_lane = static_cast<uint32_t>(lrow * L::ARB + lm_col(lane) * 2);
   const int64_t ch_out = ch_base + warp * 16 + 2 * q;
 
   uint32_t bw[S][KT][4];  // basis fragments for W = alpha . basis_s (B operand, 2 channel n-tiles)
   for (int64_t it = i0; it < i1; ++it) {
     const int cur = static_cast<int>((it - i0) & 1);
-    if (it + 1 < i1) {
+    const uint32_t parity = static_cast<uint32_t>(((it - i0) >> 1) & 1);
+    if (threadIdx.x == 0 && it + 1 < i1) {
       int64_t ss, se, r0, r1;
+      const uint32_t nbar = sm.bar + 8 * (cur ^ 1);
       if (a.rm.item(it + 1, ss, se, r0, r1))
-        load_tile<L, false, ACT>(a, stages + (cur ^ 1) * L::stage_bytes, ss, se, r0, r1, ch_base);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+        issue_tile<L, false>(&xmap, nullptr, &amap, sm.stages + (cur ^ 1) * L::stage_bytes, nbar, r0, ch_base);
+      else
+        mbar_arrive(nbar);
     }
-    __syncthreads();
+    const bool landed = mbar_wait(sm.bar + 8 * cur, parity);
+    if (__syncthreads_or(!landed)) {
+      if (threadIdx.x == 0) {
+        atomicOr(&g_conv_status, kStatusWaitTimeout);
+        mbar_wait(sm.bar + 8 * cur, parity);
+        if (it + 1 < i1) mbar_wait(sm.bar + 8 * (cur ^ 1), parity ^ static_cast<uint32_t>(cur));
+      }
+      return;
+    }
     if (it == i0) {
+      cp_async_wait<0>();
+      __syncthreads();
 #pragma unroll
       for (int s = 0; s < S; ++s)
 #pragma unroll
         for (int kt = 0; kt < KT; ++kt)
-          ldsm_x4_t(smem_addr(basis_s + (s * L::KP + kt * 16 + lm_row(lane)) * kRowB +
-                              (warp * 16 + lm_col(lane)) * 2),
+          ldsm_x4_t(smem_addr(sm.head + (s * L::KP + kt * 16 + lrow) * kRowB + (warp * 16 + lm_col(lane)) * 2),
                     bw[s][kt]);
     }
     int64_t ss, se, r0, r1;
     if (a.rm.item(it, ss, se, r0, r1)) {
-      const uint32_t x_s = smem_addr(stages + cur * L::stage_bytes);
+      char* stage_p = sm.stages_p + cur * L::stage_bytes;
+      const int zx = static_cast<int>(std::min<int64_t>(std::max<int64_t>(ss - (r0 - kHalo), 0), L::XR));
+      if (zx > 0) {  // uniform across the CTA
+        zero_rows<L>(stage_p, zx, L::FR);
+        __syncthreads();
+      }
+      const uint32_t x_s = sm.stages + cur * L::stage_bytes;
       const uint32_t a_s = x_s + L::x_bytes;
       const int rows = static_cast<int>(r1 - r0);
       const int nb = (rows + 15) >> 4;
@@ -197,14 +247,17 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
 #pragma unroll
         for (int s = 0; s < S; ++s) {
           const int j = S - 1 - s;
-          float w[2][4] = {};
+          float w[2][4];
+          mma_bf16_z(w[0], af[0], bw[s][0][0], bw[s][0][1]);
+          mma_bf16_z(w[1], af[0], bw[s][0][2], bw[s][0][3]);
 #pragma unroll
-          for (int kt = 0; kt < KT; ++kt) {
+          for (int kt = 1; kt < KT; ++kt) {
             mma_bf16(w[0], af[kt], bw[s][kt][0], bw[s][kt][1]);
             mma_bf16(w[1], af[kt], bw[s][kt][2], bw[s][kt][3]);
           }
           uint32_t xr[4];
-          ldsm_x4(x_s + (kHalo + 16 * b - j) * kRowB + x_lane, xr);
+          const int xrow = kHalo + 16 * b - j + lrow;
+          ldsm_x4(x_s + x_box + xrow * 128 + (((x_chunk ^ xrow) & 7) << 4), xr);
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
             ffma2(acc[nt][0], acc[nt][1], w[nt][0], w[nt][1], bf_lo(xr[2 * nt]), bf_hi(xr[2 * nt]));
@@ -227,22 +280,24 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
         }
       }
     }
-    __syncthreads();
+    __syncthreads();  // the stage is refilled by the next iteration's issue
   }
 }
 
 // ------------------------------------------------------------------ backward
 
 template <int KT, int S, bool ACT>
-__global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_blocks)) k_tc_bwd(TcArgs a) {
+__global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_blocks))
+    k_tc_bwd(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap dymap,
+             const __grid_constant__ CUtensorMap amap, TcArgs a) {
   using L = Layout<KT, S, ACT, true>;
   constexpr int KP = L::KP;
   constexpr bool BREG = L::BREG;
-  extern __shared__ __align__(128) char smem[];
-  char* basis_s = smem;
-  float* red_s = reinterpret_cast<float*>(smem + (BREG ? 0 : L::basis_bytes));  // [2][8 warps][16][KP]
-  char* stages = smem + L::head_bytes;
-  char* dz_s = stages + 2 * L::stage_bytes;
+  extern __shared__ __align__(1024) char smem_raw[];
+  const Smem<L> sm(smem_raw);
+  char* basis_s = sm.head;
+  float* red_s = reinterpret_cast<float*>(sm.head + (BREG ? 0 : L::basis_bytes));  // [2][8 warps][16][KP]
+  char* dz_s = sm.dz;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int64_t slice = blockIdx.x;
@@ -253,42 +308,68 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
   const bool want_dx = a.dx != nullptr;
   const int ch_w = warp * 16;  // this warp's channel offset inside the slice
 
-  // per-lane shared-memory offsets of ldmatrix row addresses
+  // per-lane constants: basis rows (padded, unswizzled), alpha rows (dense), and the
+  // swizzled x / dy boxes holding this warp's 16 channels (chunks 2*(warp&3)+{0,1})
   const uint32_t basis_base = smem_addr(basis_s);
-  const uint32_t a_lane = static_cast<uint32_t>(lm_row(lane) * L::ARB + lm_col(lane) * 2);
-  const uint32_t c_lane = static_cast<uint32_t>(lm_row(lane) * kRowB + (ch_w + lm_col(lane)) * 2);
-  const uint32_t bt_lane = static_cast<uint32_t>(lm_row(lane) * kRowB + (ch_w + lm_col(lane)) * 2);
+  const int lrow = lm_row(lane);
+  const uint32_t a_lane = static_cast<uint32_t>(lrow * L::ARB + lm_col(lane) * 2);
+  const uint32_t bt_lane = static_cast<uint32_t>(lrow * kRowB + (ch_w + lm_col(lane)) * 2);
   const uint32_t bn_lane =
       static_cast<uint32_t>(((lane & 7) + (lane >> 4) * 8) * kRowB + (ch_w + ((lane >> 3) & 1) * 8) * 2);
+  const uint32_t x_box = static_cast<uint32_t>((warp >> 2) * L::xbox);
+  const uint32_t dy_box = static_cast<uint32_t>(L::x_bytes + (warp >> 2) * L::dybox);
+  const int m_chunk = 2 * (warp & 3) + (lane >> 4);
 
-  float dba[S][2 * KT][4] = {};              // dbasis^T accumulators: (ch g | g+8) x (k 8kn + 2q..)
-  uint32_t bw[BREG ? S : 1][KT][4];          // basis, B operand of W = alpha . basis_s
-  uint32_t bd[BREG ? S : 1][KT][4];          // basis^T, B operand of dalpha = m . basis_s^T
+  float dba[S][2 * KT][4] = {};      // dbasis^T accumulators: (ch g | g+8) x (k 8kn + 2q..)
+  uint32_t bw[BREG ? S : 1][KT][4];  // basis, B operand of W = alpha . basis_s
+  uint32_t bd[BREG ? S : 1][KT][4];  // basis^T, B operand of dalpha = m . basis_s^T
 
   if (i0 < i1) {
-    load_basis<L, true, ACT>(a, basis_s, ch_base, S);
-    {
-      int64_t ss, se, r0, r1;
-      if (a.rm.item(i0, ss, se, r0, r1)) load_tile<L, true, ACT>(a, stages, ss, se, r0, r1, ch_base);
+    if (threadIdx.x == 0) {
+      tma_prefetch_desc(&xmap);
+      tma_prefetch_desc(&dymap);
+      tma_prefetch_desc(&amap);
+      mbar_init(sm.bar, 1);
+      mbar_init(sm.bar + 8, 1);
+      fence_mbar_init();
     }
+    load_basis<L, true>(a, basis_s, ch_base, S);
     cp_async_commit();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int64_t ss, se, r0, r1;
+      if (a.rm.item(i0, ss, se, r0, r1))
+        issue_tile<L, true>(&xmap, &dymap, &amap, sm.stages, sm.bar, r0, ch_base);
+      else
+        mbar_arrive(sm.bar);
+    }
   }
   int red_buf = 0;
 
   for (int64_t it = i0; it < i1; ++it) {
     const int cur = static_cast<int>((it - i0) & 1);
-    if (it + 1 < i1) {
+    const uint32_t parity = static_cast<uint32_t>(((it - i0) >> 1) & 1);
+    if (threadIdx.x == 0 && it + 1 < i1) {
       int64_t ss, se, r0, r1;
+      const uint32_t nbar = sm.bar + 8 * (cur ^ 1);
       if (a.rm.item(it + 1, ss, se, r0, r1))
-        load_tile<L, true, ACT>(a, stages + (cur ^ 1) * L::stage_bytes, ss, se, r0, r1, ch_base);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+        issue_tile<L, true>(&xmap, &dymap, &amap, sm.stages + (cur ^ 1) * L::stage_bytes, nbar, r0, ch_base);
+      else
+        mbar_arrive(nbar);
     }
-    __syncthreads();
-    if constexpr (BREG) {
-      if (it == i0) {
+    const bool landed = mbar_wait(sm.bar + 8 * cur, parity);
+    if (__syncthreads_or(!landed)) {
+      if (threadIdx.x == 0) {
+        atomicOr(&g_conv_status, kStatusWaitTimeout);
+        mbar_wait(sm.bar + 8 * cur, parity);
+        if (it + 1 < i1) mbar_wait(sm.bar + 8 * (cur ^ 1), parity ^ static_cast<uint32_t>(cur));
+      }
+      return;
+    }
+    if (it == i0) {
+      cp_async_wait<0>();
+      __syncthreads();
+      if constexpr (BREG) {
 #pragma unroll
         for (int s = 0; s < (BREG ? S : 1); ++s)
 #pragma unroll
@@ -301,30 +382,48 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
     }
     int64_t ss, se, r0, r1;
     const bool valid = a.rm.item(it, ss, se, r0, r1);
-    const uint32_t x_s = smem_addr(stages + cur * L::stage_bytes);
-    const uint32_t dy_s = x_s + L::x_bytes;
-    const uint32_t a_s = dy_s + L::dy_bytes;
-    const char* dy_p = stages + cur * L::stage_bytes + L::x_bytes;
+    char* stage_p = sm.stages_p + cur * L::stage_bytes;
+    const uint32_t x_s = sm.stages + cur * L::stage_bytes;
+    const uint32_t a_s = x_s + L::x_bytes + L::dy_bytes;
     const int rows = valid ? static_cast<int>(r1 - r0) : 0;
+    if (valid) {
+      const int zx = static_cast<int>(std::min<int64_t>(std::max<int64_t>(ss - (r0 - kHalo), 0), L::XR));
+      const int zdy = static_cast<int>(std::min<int64_t>(std::max<int64_t>(se - r0, 0), L::FR));
+      if (zx > 0 || zdy < L::FR) {  // uniform across the CTA
+        zero_rows<L>(stage_p, zx, zdy);
+        __syncthreads();
+      }
+    }
 
+    // swizzled shared address of the ldmatrix row of this lane at tile row `row0 + lrow`
+    auto x_addr = [&](int row0) {
+      const int r = row0 + lrow;
+      return x_s + x_box + r * 128 + (((m_chunk ^ r) & 7) << 4);
+    };
+    auto dy_addr = [&](int row0) {
+      const int r = row0 + lrow;
+      return x_s + dy_box + r * 128 + (((m_chunk ^ r) & 7) << 4);
+    };
     // W fragments (C layout) for alpha rows starting at tile row ar, tap s.
     auto w_frag = [&](int ar, int s, float (&w)[2][4]) {
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) w[nt][e] = 0.f;
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt) {
         uint32_t af[4];
         ldsm_x4(a_s + ar * L::ARB + kt * 32 + a_lane, af);
+        uint32_t b0, b1, b2, b3;
         if constexpr (BREG) {
-          mma_bf16(w[0], af, bw[s][kt][0], bw[s][kt][1]);
-          mma_bf16(w[1], af, bw[s][kt][2], bw[s][kt][3]);
+          b0 = bw[s][kt][0], b1 = bw[s][kt][1], b2 = bw[s][kt][2], b3 = bw[s][kt][3];
         } else {
           uint32_t bf[4];
           ldsm_x4_t(basis_base + (s * KP + kt * 16) * kRowB + bt_lane, bf);
-          mma_bf16(w[0], af, bf[0], bf[1]);
-          mma_bf16(w[1], af, bf[2], bf[3]);
+          b0 = bf[0], b1 = bf[1], b2 = bf[2], b3 = bf[3];
+        }
+        if (kt == 0) {
+          mma_bf16_z(w[0], af, b0, b1);
+          mma_bf16_z(w[1], af, b2, b3);
+        } else {
+          mma_bf16(w[0], af, b0, b1);
+          mma_bf16(w[1], af, b2, b3);
         }
       }
     };
@@ -334,8 +433,8 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const float2 d = *reinterpret_cast<const float2*>(dz_s + (rb + g + 8 * h) * kDzRowB +
-                                                            (ch_w + nt * 8 + 2 * q) * 4);
+          const float2 d =
+              *reinterpret_cast<const float2*>(dz_s + (rb + g + 8 * h) * kDzRowB + (ch_w + nt * 8 + 2 * q) * 4);
           v[nt][2 * h] = d.x;
           v[nt][2 * h + 1] = d.y;
         }
@@ -353,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
               float w[2][4];
               w_frag(16 * b, s, w);
               uint32_t xr[4];
-              ldsm_x4(x_s + (kHalo + 16 * b - j) * kRowB + c_lane, xr);
+              ldsm_x4(x_addr(kHalo + 16 * b - j), xr);
 #pragma unroll
               for (int nt = 0; nt < 2; ++nt) {
                 ffma2(pre[nt][0], pre[nt][1], w[nt][0], w[nt][1], bf_lo(xr[2 * nt]), bf_hi(xr[2 * nt]));
@@ -366,12 +465,13 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int row = 16 * b + g + 8 * h;
-              const int col = ch_w + nt * 8 + 2 * q;
-              const uint32_t d = *reinterpret_cast<const uint32_t*>(dy_p + row * kRowB + col * 2);
+              const int chunk = 2 * (warp & 3) + nt;  // 16-byte chunk of (row, ch_w + 8nt)
+              const uint32_t d = *reinterpret_cast<const uint32_t*>(
+                  stage_p + dy_box + row * 128 + (((chunk ^ row) & 7) << 4) + 4 * q);
               float2 o;
               o.x = bf_lo(d) * dsilu_f(pre[nt][2 * h]);
               o.y = bf_hi(d) * dsilu_f(pre[nt][2 * h + 1]);
-              *reinterpret_cast<float2*>(dz_s + row * kDzRowB + col * 4) = o;
+              *reinterpret_cast<float2*>(dz_s + row * kDzRowB + (ch_w + nt * 8 + 2 * q) * 4) = o;
             }
         }
         __syncwarp();
@@ -385,12 +485,12 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
       uint32_t ab[KT][4];  // alpha as the B operand of dbasis (tokens x bases)
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt) ldsm_x4_t(a_s + (16 * b) * L::ARB + kt * 32 + a_lane, ab[kt]);
-      uint32_t dyu[4];     // dy of this block, packed bf16 pairs (no activation)
-      float dzu[2][4];     // fp32 dz of this block (SiLU)
+      uint32_t dyu[4];  // dy of this block, packed bf16 pairs (no activation)
+      float dzu[2][4];  // fp32 dz of this block (SiLU)
       if constexpr (ACT) {
         load_dz32(16 * b, dzu);
       } else {
-        ldsm_x4(dy_s + (16 * b) * kRowB + c_lane, dyu);
+        ldsm_x4(dy_addr(16 * b), dyu);
       }
       float dxa[2][4] = {};
       float daa[2 * KT][4] = {};
@@ -410,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
             }
           } else {
             uint32_t dys[4];
-            ldsm_x4(dy_s + (16 * b + j) * kRowB + c_lane, dys);
+            ldsm_x4(dy_addr(16 * b + j), dys);
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
               ffma2(dxa[nt][0], dxa[nt][1], w[nt][0], w[nt][1], bf_lo(dys[2 * nt]), bf_hi(dys[2 * nt]));
@@ -419,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
           }
         }
         uint32_t xr[4];
-        ldsm_x4(x_s + (kHalo + 16 * b - j) * kRowB + c_lane, xr);
+        ldsm_x4(x_addr(kHalo + 16 * b - j), xr);
         uint32_t m[4];  // A operand (tokens x channels) of dalpha, rounded to bf16
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
@@ -480,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
       }
       red_buf ^= 1;
     }
-    __syncthreads();
+    __syncthreads();  // the stage is refilled by the next iteration's issue
   }
 
   // dbasis partial of this CTA: db_part[group][k][s][ch]
@@ -506,11 +606,13 @@ __global__ void k_tc_finalize(const float* __restrict__ da_part, int64_t n_slice
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float s = 0.f;
     if (i < nk) {
-      for (int64_t c = 0; c < n_slices; ++c) s += da_part[c * nk + i];
+#pragma unroll 8
+      for (int64_t c = 0; c < n_slices; ++c) s += __ldg(da_part + c * nk + i);
       st_any(dalpha, adt, i, s);
     } else {
       const int64_t j = i - nk;
-      for (int64_t g = 0; g < groups; ++g) s += db_part[g * ksd + j];
+#pragma unroll 8
+      for (int64_t g = 0; g < groups; ++g) s += __ldg(db_part + g * ksd + j);
       st_any(dbasis, bdt, j, s);
     }
   }
@@ -545,8 +647,7 @@ Plan make_plan(const moc_problem& p, int ctas_per_sm) {
 // Raises the dynamic shared-memory limit of `kern` once per device (`configured` is owned
 // by the caller's template instantiation, i.e. one flag set per kernel), so launches
 // captured into a CUDA graph later make no attribute calls.
-template <typename Kern>
-int launch(Kern kern, bool (&configured)[64], dim3 grid, int smem, cudaStream_t st, const TcArgs& args) {
+int configure(const void* kern, bool (&configured)[64], int smem) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return note_cuda(e);
@@ -555,25 +656,46 @@ int launch(Kern kern, bool (&configured)[64], dim3 grid, int smem, cudaStream_t 
     if (e != cudaSuccess) return note_cuda(e);
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  kern<<<grid, kThreads, smem, st>>>(args);
-  note_launch();
-  return note_cuda(cudaGetLastError());
+  return MOC_OK;
+}
+
+struct Maps {
+  CUtensorMap x, dy, a;
+};
+
+template <class L, bool BWD>
+int make_maps(const moc_problem& p, const void* x, const void* dy, const void* alpha, Maps& m) {
+  const uint64_t D = static_cast<uint64_t>(p.dim), N = static_cast<uint64_t>(p.n_tokens);
+  int rc = make_tmap_bf16_2d(&m.x, x, D, N, D * 2, 64, L::XR, true);
+  if (rc == MOC_OK && BWD) rc = make_tmap_bf16_2d(&m.dy, dy, D, N, D * 2, 64, L::FR, true);
+  if (rc == MOC_OK)
+    rc = make_tmap_bf16_2d(&m.a, alpha, static_cast<uint64_t>(p.n_bases), N, static_cast<uint64_t>(p.n_bases) * 2,
+                           L::KP, L::AR, false);
+  return rc;
 }
 
 template <int KT, int S, bool ACT>
-int fwd_inst(const moc_problem& p, TcArgs& args, cudaStream_t st) {
+int fwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alpha, cudaStream_t st) {
   using L = Layout<KT, S, ACT, false>;
   const Plan pl = make_plan(p, L::min_blocks);
   args.rm = pl.rm;
   args.items_per_group = pl.ipg;
   if (pl.rm.n_items() == 0) return MOC_OK;
   static bool configured[64] = {};
-  return launch(k_tc_fwd<KT, S, ACT>, configured, dim3(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups)),
-                L::total, st, args);
+  int rc = configure(reinterpret_cast<const void*>(k_tc_fwd<KT, S, ACT>), configured, L::total);
+  if (rc != MOC_OK) return rc;
+  Maps m;
+  rc = make_maps<L, false>(p, x, nullptr, alpha, m);
+  if (rc != MOC_OK) return rc;
+  k_tc_fwd<KT, S, ACT><<<dim3(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups)), kThreads, L::total,
+                         st>>>(m.x, m.a, args);
+  note_launch();
+  return note_cuda(cudaGetLastError());
 }
 
 template <int KT, int S, bool ACT>
-int bwd_inst(const moc_problem& p, TcArgs& args, void* dalpha, void* dbasis, cudaStream_t st) {
+int bwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alpha, const void* dy, void* dalpha,
+             void* dbasis, cudaStream_t st) {
   using L = Layout<KT, S, ACT, true>;
   static_assert(L::min_blocks == ((L::BREG && !ACT && KT == 1) ? 2 : 1), "bwd_min_blocks() mirrors Layout::min_blocks");
   const Plan pl = make_plan(p, L::min_blocks);
@@ -582,8 +704,15 @@ int bwd_inst(const moc_problem& p, TcArgs& args, void* dalpha, void* dbasis, cud
   const int64_t nk = p.n_tokens * p.n_bases;
   const int64_t ksd = static_cast<int64_t>(p.n_bases) * p.kernel_size * p.dim;
   static bool configured[64] = {};
-  int rc = launch(k_tc_bwd<KT, S, ACT>, configured, dim3(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups)),
-                  L::total, st, args);
+  int rc = configure(reinterpret_cast<const void*>(k_tc_bwd<KT, S, ACT>), configured, L::total);
+  if (rc != MOC_OK) return rc;
+  Maps m;
+  rc = make_maps<L, true>(p, x, dy, alpha, m);
+  if (rc != MOC_OK) return rc;
+  k_tc_bwd<KT, S, ACT><<<dim3(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups)), kThreads, L::total,
+                         st>>>(m.x, m.dy, m.a, args);
+  note_launch();
+  rc = note_cuda(cudaGetLastError());
   if (rc != MOC_OK) return rc;
   const int64_t blocks = std::min<int64_t>(ceil_div(nk + ksd, 256), 8 * sm_count());
   k_tc_finalize<<<static_cast<unsigned>(blocks), 256, 0, st>>>(args.da_part, pl.slices, nk, dalpha, p.alpha_dtype,
@@ -596,9 +725,9 @@ template <template <int, int, bool> class F, typename... Args>
 int dispatch(const moc_problem& p, Args&&... args) {
   const int KT = p.n_bases <= 16 ? 1 : 2;
   const bool act = p.activation != 0;
-#define MOC_TC_CASE(kt, s)                                                        \
-  if (KT == kt && p.kernel_size == s)                                             \
-    return act ? F<kt, s, true>::run(p, std::forward<Args>(args)...)              \
+#define MOC_TC_CASE(kt, s)                                           \
+  if (KT == kt && p.kernel_size == s)                                \
+    return act ? F<kt, s, true>::run(p, std::forward<Args>(args)...) \
                : F<kt, s, false>::run(p, std::forward<Args>(args)...);
   MOC_TC_CASE(1, 1) MOC_TC_CASE(1, 2) MOC_TC_CASE(1, 3) MOC_TC_CASE(1, 4)
   MOC_TC_CASE(1, 5) MOC_TC_CASE(1, 6) MOC_TC_CASE(1, 7) MOC_TC_CASE(1, 8)
@@ -609,12 +738,15 @@ int dispatch(const moc_problem& p, Args&&... args) {
 
 template <int KT, int S, bool ACT>
 struct FwdRun {
-  static int run(const moc_problem& p, TcArgs& args, cudaStream_t st) { return fwd_inst<KT, S, ACT>(p, args, st); }
+  static int run(const moc_problem& p, TcArgs& args, const void* x, const void* alpha, cudaStream_t st) {
+    return fwd_inst<KT, S, ACT>(p, args, x, alpha, st);
+  }
 };
 template <int KT, int S, bool ACT>
 struct BwdRun {
-  static int run(const moc_problem& p, TcArgs& args, void* da, void* db, cudaStream_t st) {
-    return bwd_inst<KT, S, ACT>(p, args, da, db, st);
+  static int run(const moc_problem& p, TcArgs& args, const void* x, const void* alpha, const void* dy, void* da,
+                 void* db, cudaStream_t st) {
+    return bwd_inst<KT, S, ACT>(p, args, x, alpha, dy, da, db, st);
   }
 };
 
@@ -646,6 +778,8 @@ bool tc_conv_supported(const moc_problem& p) {
   if (p.dim % 8 != 0) return false;
   if (p.cu_seqlens != nullptr && p.chunk_size != kTile) return false;
   if (ceil_div(p.dim, kBD) > 65535) return false;
+  // TMA coordinates are 32-bit
+  if (p.n_tokens > (int64_t{1} << 31) - 1024 || p.dim > (int64_t{1} << 31) - 1024) return false;
   return true;
 }
 
@@ -655,12 +789,10 @@ int tc_forward(const moc_problem& p, const void* x, const void* alpha, const voi
   TcArgs args{};
   args.D = p.dim;
   args.K = p.n_bases;
-  args.x = static_cast<const bf16*>(x);
-  args.alpha = static_cast<const bf16*>(alpha);
   args.basis = static_cast<const bf16*>(basis);
   args.out = static_cast<bf16*>(out);
   args.n_tokens = p.n_tokens;
-  return dispatch<FwdRun>(p, args, st);
+  return dispatch<FwdRun>(p, args, x, alpha, st);
 }
 
 size_t tc_backward_ws(const moc_problem& p) {
@@ -681,15 +813,25 @@ int tc_backward(const moc_problem& p, const void* x, const void* alpha, const vo
   TcArgs args{};
   args.D = p.dim;
   args.K = p.n_bases;
-  args.x = static_cast<const bf16*>(x);
-  args.alpha = static_cast<const bf16*>(alpha);
   args.basis = static_cast<const bf16*>(basis);
-  args.dy = static_cast<const bf16*>(dy);
   args.dx = static_cast<bf16*>(dx);
   args.da_part = static_cast<float*>(ws);
   args.db_part = reinterpret_cast<float*>(static_cast<char*>(ws) + da);
   args.n_tokens = p.n_tokens;
-  return dispatch<BwdRun>(p, args, dalpha, dbasis, st);
+  return dispatch<BwdRun>(p, args, x, alpha, dy, dalpha, dbasis, st);
+}
+
+int conv_status(int* out, bool clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_conv_status, sizeof(int));
+  if (e != cudaSuccess) return note_cuda(e);
+  if (clear && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_conv_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return note_cuda(e);
+  }
+  *out = v;
+  return MOC_OK;
 }
 
 }  // namespace moc

@@ -59,6 +59,8 @@ SIGNATURES = {
     "moc_last_cuda_error": (ctypes.c_char_p, []),
     "moc_set_kernel_path": (ctypes.c_int, [ctypes.c_int]),
     "moc_launch_count": (ctypes.c_uint64, []),
+    "moc_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    "moc_wait_timeout_probe": (ctypes.c_int, [ctypes.c_uint32, _P]),
     "moc_forward": (ctypes.c_int, [_PROB, _P, _P, _P, _P, _P]),
     "moc_backward_workspace_bytes": (_SZ, [_PROB]),
     "moc_backward": (ctypes.c_int, [_PROB, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
@@ -140,6 +142,13 @@ def stream_of(device: torch.device) -> int:
 def launch_count() -> int:
     """Kernels launched by the library so far in this process."""
     return int(load().moc_launch_count())
+
+
+def device_status(clear: bool = False) -> int:
+    """OR of the MOC_STATUS_* bits the staging kernels recorded (synchronous read)."""
+    v = ctypes.c_int(0)
+    check(load().moc_device_status(ctypes.byref(v), int(clear)), "moc_device_status")
+    return v.value
 
 
 def set_kernel_path(path: int) -> None:

@@ -1,0 +1,36 @@
+"""Failure detection on the GPU without a fault: the bounded mbarrier wait used by the
+TMA-staged kernels gives up after its poll budget, records MOC_STATUS_WAIT_TIMEOUT in
+the device status word, and returns; the CUDA context stays usable."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from moc import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def test_wait_timeout_is_reported_not_hung():
+    lib = _lib.load()
+    _lib.device_status(clear=True)
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.moc_wait_timeout_probe(2000, stream), "moc_wait_timeout_probe")
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) & 1
+    assert _lib.device_status() == 0
+    t = torch.arange(8, device="cuda", dtype=torch.float32)
+    assert t.sum().item() == 28.0  # context still healthy
+
+
+def test_normal_kernels_record_no_timeouts():
+    from moc import MoC
+
+    _lib.device_status(clear=True)
+    m = MoC(256, 256, 4, 16).cuda().bfloat16()
+    x = torch.randn(2, 512, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    z = torch.randn(2, 512, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y, _ = m(x, z)
+    y.float().sum().backward()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
