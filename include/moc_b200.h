@@ -46,6 +46,7 @@ extern "C" {
 #define MOC_ERR_MISALIGNED 4
 #define MOC_ERR_WORKSPACE_TOO_SMALL 5
 #define MOC_ERR_CUDA 6
+#define MOC_ERR_SCRATCH_LIMIT 7
 
 /* Shape and routing of one convolution problem.
  * Fixed length: batch > 0, seq_len > 0, n_tokens = batch*seq_len, varlen fields zero/NULL.
@@ -154,6 +155,28 @@ int moc_router_backward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_
                         const void* alpha, const void* dalpha, int32_t dalpha_dtype,
                         void* dz, void* dweight, void* workspace, size_t workspace_bytes,
                         void* stream);
+
+/* Router backward that allocates nothing, for callers that cannot call cudaMalloc (or
+ * hand this library any allocator): hosts that reach the kernels only through this C ABI
+ * with tensors they do not own, or code that must not allocate once it is running, such
+ * as a server that plans all device memory at start-up.  Same arguments and results as
+ * moc_router_backward for bf16 problems the tensor-core path supports (n_bases % 8 == 0,
+ * n_bases <= 32, z_dim % 8 == 0), without the workspace: the per-CTA dweight partials go
+ * to a fixed MOC_NOALLOC_SCRATCH_BYTES array in the library's device memory, which every
+ * GPU that loads the library holds until the process exits.  Problems whose partials do
+ * not fit return MOC_ERR_SCRATCH_LIMIT; other shapes and dtypes return
+ * MOC_ERR_UNSUPPORTED_SHAPE / MOC_ERR_UNSUPPORTED_DTYPE.  The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress), so make that first call before
+ * any stream capture on that device.  All calls share the one array: calls that can
+ * overlap on the GPU (different streams, or different host threads) race on it and must
+ * be serialised by the caller.  Nothing in it needs to start at zero; every call rewrites
+ * the partials it reads.  No counterpart in the reference (its router backward is PyTorch
+ * autograd, which allocates through the caching allocator). */
+#define MOC_NOALLOC_SCRATCH_BYTES (8u << 20)
+int moc_router_backward_noalloc(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t dtype,
+                                int32_t router_act, const void* z, const void* weight,
+                                const void* alpha, const void* dalpha, int32_t dalpha_dtype,
+                                void* dz, void* dweight, void* stream);
 
 /* Device-side chunk index builder for packed varlen (no host sync): fills
  * chunk_indices [n_chunks, 2] int32 with (seq_id, chunk_in_seq) for every

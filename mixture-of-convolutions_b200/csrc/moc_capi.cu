@@ -96,6 +96,8 @@ const char* moc_error_string(int code) {
     case MOC_ERR_MISALIGNED: return "pointer not aligned for vector access";
     case MOC_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
     case MOC_ERR_CUDA: return "CUDA error (see moc_last_cuda_error)";
+    case MOC_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the fixed MOC_NOALLOC_SCRATCH_BYTES array (use the workspace entry point)";
     default: return "unknown error code";
   }
 }
@@ -210,6 +212,20 @@ int moc_router_backward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_
   if (workspace_bytes < simt_router_backward_ws(n_tokens, z_dim, n_bases)) return MOC_ERR_WORKSPACE_TOO_SMALL;
   return simt_router_backward(n_tokens, z_dim, n_bases, dtype, router_act, z, weight, alpha, dalpha, dalpha_dtype,
                               dz, dweight, workspace, workspace_bytes, st);
+}
+
+int moc_router_backward_noalloc(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t dtype, int32_t router_act,
+                                const void* z, const void* weight, const void* alpha, const void* dalpha,
+                                int32_t dalpha_dtype, void* dz, void* dweight, void* stream) {
+  if (!valid_float_dtype(dtype) || !valid_float_dtype(dalpha_dtype)) return MOC_ERR_UNSUPPORTED_DTYPE;
+  if (n_tokens < 0 || z_dim <= 0 || n_bases <= 0 || (router_act != 0 && router_act != 1))
+    return MOC_ERR_INVALID_ARGUMENT;
+  if (dtype != MOC_DTYPE_BF16) return MOC_ERR_UNSUPPORTED_DTYPE;
+  if (n_tokens == 0) return MOC_OK;
+  if (!tc_router_supported(n_tokens, z_dim, n_bases, dtype)) return MOC_ERR_UNSUPPORTED_SHAPE;
+  if (!z || !weight || !alpha || !dalpha) return MOC_ERR_INVALID_ARGUMENT;
+  return tc_router_backward_noalloc(n_tokens, z_dim, n_bases, router_act, z, weight, alpha, dalpha, dalpha_dtype, dz,
+                                    dweight, static_cast<cudaStream_t>(stream));
 }
 
 int moc_prepare_chunk_indices(const void* cu_seqlens, int32_t cu_seqlens_dtype, int64_t n_seqs, int32_t chunk_size,

@@ -46,6 +46,10 @@ int tc_router_backward(int64_t N, int64_t Dz, int K, int act, const void* z, con
                        const void* dalpha, int da_dtype, void* dz, void* dw, void* ws, size_t ws_bytes,
                        cudaStream_t st);
 
+// router backward with its scratch in a fixed device array (moc_router_tc.cu)
+int tc_router_backward_noalloc(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, const void* alpha,
+                               const void* dalpha, int da_dtype, void* dz, void* dw, cudaStream_t st);
+
 // device status words of the TMA-staged kernels (bounded-wait timeouts), read/cleared
 // by moc_device_status(); and a probe kernel that exercises the timeout path.
 int router_status(int* out, bool clear);

@@ -14,6 +14,7 @@
 //             keeps dW^T for its slice in registers; a second kernel adds the per-CTA dW
 //             partials in a fixed order (deterministic).
 #include <algorithm>
+#include <mutex>
 
 #include "moc_common.cuh"
 #include "moc_internal.h"
@@ -440,6 +441,39 @@ int tc_router_backward(int64_t N, int64_t Dz, int K, int act, const void* z, con
   bwd_plan(N, Dz, slices, groups, tpg);
   a.tiles_per_group = tpg;
   return K <= 16 ? bwd_kt<1>(a, slices, groups, dw, st) : bwd_kt<2>(a, slices, groups, dw, st);
+}
+
+// ------------------------------------------------------------------ no-allocation variant
+
+// Fixed scratch for tc_router_backward_noalloc: the dweight partials of one call.  It is
+// part of the library image, so no call allocates; every call reuses (and overwrites) it.
+static __device__ __align__(256) float g_noalloc_scratch[MOC_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+int tc_router_backward_noalloc(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, const void* alpha,
+                               const void* dalpha, int da_dtype, void* dz, void* dw, cudaStream_t st) {
+  if (tc_router_backward_ws(N, Dz, K) > MOC_NOALLOC_SCRATCH_BYTES) return MOC_ERR_SCRATCH_LIMIT;
+  // Device address of the array, looked up once per device with that device current
+  // (host code cannot use the symbol itself: on the host it names a stand-in, not device memory).
+  static std::mutex lock;
+  static void* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return note_cuda(e);
+  if (dev < 0 || dev >= 64) return MOC_ERR_INVALID_ARGUMENT;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> guard(lock);
+    if (addr[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess) return note_cuda(e);
+      addr[dev] = p;
+    }
+    scratch = addr[dev];
+  }
+  // Every dweight partial is written before the reduction reads it, so nothing is cleared.
+  return tc_router_backward(N, Dz, K, act, z, w, alpha, dalpha, da_dtype, dz, dw, scratch,
+                            MOC_NOALLOC_SCRATCH_BYTES, st);
 }
 
 int router_status(int* out, bool clear) {

@@ -74,6 +74,10 @@ SIGNATURES = {
         ctypes.c_int,
         [_I64, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _P, _P, _P, _SZ, _P],
     ),
+    "moc_router_backward_noalloc": (
+        ctypes.c_int,
+        [_I64, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _P, _P, _P],
+    ),
     "moc_prepare_chunk_indices": (ctypes.c_int, [_P, _I32, _I64, _I32, _P, _I64, _P]),
 }
 
