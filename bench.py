@@ -150,12 +150,12 @@ class ClockSampler:
 def make_module_and_inputs(cfg: dict, rank: int, device: torch.device):
     from moc import MoC
 
-    torch.manual_seed(1234 + rank)
+    torch.manual_seed(1234)  # the same parameters on every rank; data differs per rank
     m = MoC(dim=cfg["D"], z_dim=cfg["Dz"], kernel_size=cfg["S"], k=cfg["K"], activation=cfg["activation"],
             init_std=cfg["init_std"], router_activation=cfg["router"])
-    g = torch.Generator().manual_seed(4321 + rank)
     with torch.no_grad():
-        m.router.copy_(torch.randn(cfg["K"], cfg["Dz"], generator=g) * cfg["router_std"])
+        m.router.copy_(torch.randn(cfg["K"], cfg["Dz"], generator=torch.Generator().manual_seed(4321)) * cfg["router_std"])
+    g = torch.Generator().manual_seed(4321 + 1 + rank)
     m = m.to(device=device, dtype=torch.bfloat16)
     shape = (cfg["B"], cfg["T"])
     host = {
@@ -170,15 +170,6 @@ def train_step(m, x, z, dy):
     y, _ = m(x, z)
     grads = torch.autograd.grad(y, (x, z, m.conv_bases, m.router), dy)
     return y, grads
-
-
-def allreduce_grads(grads, flat: torch.Tensor) -> None:
-    """Sum [dconv_bases | drouter] over ranks in one fp32 NCCL all-reduce."""
-    dbasis, drouter = grads[2], grads[3]
-    n0 = dbasis.numel()
-    flat[:n0].copy_(dbasis.reshape(-1))
-    flat[n0:].copy_(drouter.reshape(-1))
-    dist.all_reduce(flat)
 
 
 def time_region(fn, steps: int, stream: torch.cuda.Stream) -> float:
@@ -291,7 +282,7 @@ def main() -> None:
         run_reference(args, rank, world)
         return
 
-    from moc import _lib
+    from moc import _lib, dp
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -304,8 +295,7 @@ def main() -> None:
     x = host["x"].to(device).requires_grad_()
     z = host["z"].to(device).requires_grad_()
     dy = host["dy"].to(device)
-    n_flat = m.conv_bases.numel() + m.router.numel()
-    flat = torch.empty(n_flat, dtype=torch.float32, device=device)
+    reducer = dp.GradAllReduce([m.conv_bases, m.router]) if world > 1 else None
 
     # --- device-resident step, captured in a CUDA graph
     side = torch.cuda.Stream(device)
@@ -328,7 +318,7 @@ def main() -> None:
     def graph_step():
         graph.replay()
         if world > 1:
-            allreduce_grads(g_grads, flat)
+            reducer(g_grads[2:])
 
     for _ in range(args.warmup):
         graph_step()
@@ -361,7 +351,7 @@ def main() -> None:
         zg = zd.detach().requires_grad_()
         y, grads = train_step(m, xg, zg, dyd)
         if world > 1:
-            allreduce_grads(grads, flat)
+            reducer(grads[2:])
         for name, t in (("y", y), ("dx", grads[0]), ("dz", grads[1]), ("dbasis", grads[2]),
                         ("drouter", grads[3])):
             out_host[name].copy_(t.detach(), non_blocking=True)

@@ -1,0 +1,93 @@
+"""Data parallelism for the MoC module: whole sequences per rank, one collective per step.
+
+Every sequence is independent and the causal halo (kernel_size - 1 tokens) never
+crosses a sequence boundary, so a rank that owns whole sequences computes its part of
+the router, the convolution and every activation gradient without communication.  The
+one exchange per step is the sum over ranks of the parameter gradients, conv_bases
+[K, S, D] and router [K, Dz]: both are flattened into one fp32 buffer and summed by a
+single all-reduce (NCCL on GPUs, gloo on CPU).  x, z, y, dx and dz never leave their GPU.
+
+The reference trains in one process (its kernels are per-device); this module is the
+scaling layer of this build, used by bench.py for the multi-GPU runs.
+"""
+from __future__ import annotations
+
+from typing import Iterable, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+def shard_fixed(batch: int, rank: int, world: int) -> slice:
+    """The sequences [start, stop) of a fixed-length batch owned by `rank`: contiguous
+    blocks, the first `batch % world` ranks holding one sequence more."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if batch < 0:
+        raise ValueError("batch must be non-negative")
+    base, extra = divmod(batch, world)
+    start = rank * base + min(rank, extra)
+    return slice(start, start + base + (1 if rank < extra else 0))
+
+
+def shard_varlen(cu_seqlens: Sequence[int] | torch.Tensor, rank: int, world: int):
+    """Split a packed varlen batch into `world` contiguous runs of whole sequences,
+    balanced by token count: rank r's run ends at the sequence boundary nearest to
+    (r + 1) / world of the tokens.
+
+    Returns (tok_start, tok_stop, local_cu_seqlens): the rank's slice of the packed
+    token axis and its cu_seqlens rebased to start at 0 (int64, on the CPU)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    cu = torch.as_tensor(cu_seqlens).detach().to("cpu", torch.int64).reshape(-1)
+    if cu.numel() < 1 or int(cu[0]) != 0 or bool((cu[1:] < cu[:-1]).any()):
+        raise ValueError("cu_seqlens must start at 0 and be non-decreasing")
+    n_seqs = cu.numel() - 1
+    total = int(cu[-1])
+    cuts = [0]
+    for r in range(1, world):
+        target = total * r / world
+        j = int(torch.searchsorted(cu, torch.tensor(target, dtype=torch.float64).to(torch.int64)))
+        j = min(max(j, 0), n_seqs)
+        # the nearer of the boundaries around the target, never behind the previous cut
+        if j > 0 and abs(int(cu[j - 1]) - target) <= abs(int(cu[j]) - target):
+            j -= 1
+        cuts.append(max(j, cuts[-1]))
+    cuts.append(n_seqs)
+    s0, s1 = cuts[rank], cuts[rank + 1]
+    t0, t1 = int(cu[s0]), int(cu[s1])
+    return t0, t1, cu[s0:s1 + 1] - t0
+
+
+class GradAllReduce:
+    """Sums parameter gradients over the ranks of `group` with one all-reduce of a
+    persistent flat buffer, allocated once: fp32 for bf16 / fp16 / fp32 parameters
+    (float64 parameters keep float64)."""
+
+    def __init__(self, params: Iterable[torch.Tensor], group=None):
+        self.params = list(params)
+        if not self.params:
+            raise ValueError("no parameters to reduce")
+        dev = self.params[0].device
+        self.sizes = [p.numel() for p in self.params]
+        dtype = torch.float32
+        for p in self.params:
+            dtype = torch.promote_types(dtype, p.dtype)
+        self.flat = torch.empty(sum(self.sizes), dtype=dtype, device=dev)
+        self.group = group
+
+    def __call__(self, grads: Sequence[torch.Tensor] | None = None) -> list[torch.Tensor]:
+        """All-reduce `grads` (default: each parameter's .grad) in place; returns them."""
+        grads = [p.grad for p in self.params] if grads is None else list(grads)
+        if len(grads) != len(self.params) or any(g is None for g in grads):
+            raise ValueError("one gradient per parameter is required")
+        off = 0
+        for g, n in zip(grads, self.sizes):
+            self.flat[off:off + n].copy_(g.reshape(-1))
+            off += n
+        dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=self.group)
+        off = 0
+        for g, n in zip(grads, self.sizes):
+            g.copy_(self.flat[off:off + n].view_as(g))
+            off += n
+        return grads
