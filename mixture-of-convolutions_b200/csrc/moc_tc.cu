@@ -271,8 +271,8 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
           for (int nt = 0; nt < 2; ++nt) {
             float v0 = acc[nt][2 * h], v1 = acc[nt][2 * h + 1];
             if (ACT) {
-              v0 = silu_f(v0);
-              v1 = silu_f(v1);
+              v0 = silu_bf(v0);
+              v1 = silu_bf(v1);
             }
             if (row_ok && ch_out + nt * 8 < a.D)
               *reinterpret_cast<uint32_t*>(out_row + (16 * b + 8 * h) * a.D + nt * 8) = pack_bf16(v0, v1);
@@ -469,8 +469,8 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
               const uint32_t d = *reinterpret_cast<const uint32_t*>(
                   stage_p + dy_box + row * 128 + (((chunk ^ row) & 7) << 4) + 4 * q);
               float2 o;
-              o.x = bf_lo(d) * dsilu_f(pre[nt][2 * h]);
-              o.y = bf_hi(d) * dsilu_f(pre[nt][2 * h + 1]);
+              o.x = bf_lo(d) * dsilu_bf(pre[nt][2 * h]);
+              o.y = bf_hi(d) * dsilu_bf(pre[nt][2 * h + 1]);
               *reinterpret_cast<float2*>(dz_s + row * kDzRowB + (ch_w + nt * 8 + 2 * q) * 4) = o;
             }
         }
