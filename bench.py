@@ -166,9 +166,13 @@ def make_module_and_inputs(cfg: dict, rank: int, device: torch.device):
     return m, host
 
 
-def train_step(m, x, z, dy):
+def train_step(m, x, z, dy, reducer=None):
+    """Forward + backward of the module; with `reducer` (N > 1) the parameter gradients
+    come back summed over ranks by one all-reduce."""
     y, _ = m(x, z)
     grads = torch.autograd.grad(y, (x, z, m.conv_bases, m.router), dy)
+    if reducer is not None:
+        reducer(grads[2:])
     return y, grads
 
 
@@ -242,6 +246,15 @@ def cpu_baseline(cfg: dict, iters: int = 2, seq_tokens: int = 2048) -> dict:
             "sec_per_iter": t}
 
 
+def bench_config(cfg: dict, world: int) -> dict:
+    """The workload description both arms print."""
+    return {"workload": "config2: MoC module fwd+bwd, B=4 T=4096 D=z_dim=2048 K=16 S=4 bf16 softmax",
+            "global_batch": cfg["B"] * world, "seq_len": cfg["T"], "D": cfg["D"], "z_dim": cfg["Dz"],
+            "K": cfg["K"], "S": cfg["S"], "parallelism": f"dp{world}",
+            "l2": "inputs larger than L2 (x, z, dy = 192 MiB per rank)",
+            "timing": "CUDA graph of one step replayed K times; CUDA events; max over ranks"}
+
+
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
@@ -252,8 +265,7 @@ def run_reference(args, rank: int, world: int) -> None:
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["sec_per_iter"] * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2 MoC fwd+bwd (CPU sample)", "B": 1, "T": seq, "D": cfg["D"],
-                   "z_dim": cfg["Dz"], "K": cfg["K"], "S": cfg["S"], "router": cfg["router"]},
+        "config": bench_config(cfg, world),
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference CPU path: oracle port of moc/reference.py + router (the reference is Python; "
@@ -301,24 +313,24 @@ def main() -> None:
     side = torch.cuda.Stream(device)
     side.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(side):
-        for _ in range(args.warmup):
-            train_step(m, x, z, dy)
+        for _ in range(args.warmup):  # (N > 1: NCCL communicator set up before the capture)
+            train_step(m, x, z, dy, reducer)
     torch.cuda.current_stream(device).wait_stream(side)
     torch.cuda.synchronize()
     launches0 = _lib.launch_count()
-    train_step(m, x, z, dy)
+    train_step(m, x, z, dy, reducer)
     torch.cuda.synchronize()
     launches_per_step = _lib.launch_count() - launches0
 
+    # one graph per step: router + conv forward and backward, and for N > 1 the one
+    # all-reduce of [dconv_bases | drouter]
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        _, g_grads = train_step(m, x, z, dy)
+        _, g_grads = train_step(m, x, z, dy, reducer)
     stream = torch.cuda.current_stream(device)
 
     def graph_step():
         graph.replay()
-        if world > 1:
-            reducer(g_grads[2:])
 
     for _ in range(args.warmup):
         graph_step()
@@ -349,9 +361,7 @@ def main() -> None:
         dyd.copy_(pin["dy"], non_blocking=True)
         xg = xd.detach().requires_grad_()
         zg = zd.detach().requires_grad_()
-        y, grads = train_step(m, xg, zg, dyd)
-        if world > 1:
-            reducer(grads[2:])
+        y, grads = train_step(m, xg, zg, dyd, reducer)
         for name, t in (("y", y), ("dx", grads[0]), ("dz", grads[1]), ("dbasis", grads[2]),
                         ("drouter", grads[3])):
             out_host[name].copy_(t.detach(), non_blocking=True)
@@ -382,6 +392,11 @@ def main() -> None:
     reps = max(5, min(args.steps, 20))
     for name, fn in kernel_calls.items():
         kernel_ms[name] = graph_time(fn, reps, device)
+    allreduce_ms = None
+    if reducer is not None:  # every rank: the same collectives in the same order
+        flat = torch.zeros_like(reducer.flat)
+        barrier(world)
+        allreduce_ms = max_over_ranks(time_region(lambda: dist.all_reduce(flat), 10, stream), world)
     dominant = max(kernel_ms, key=kernel_ms.get)
     peaks = measured_peaks()
     kbytes = KERNEL_BYTES_PER_TOKEN[dominant](cfg) * N_rank
@@ -405,11 +420,7 @@ def main() -> None:
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": "config2: MoC module fwd+bwd, B=4 T=4096 D=z_dim=2048 K=16 S=4 bf16 softmax",
-                       "global_batch": cfg["B"] * world, "seq_len": cfg["T"], "D": cfg["D"], "z_dim": cfg["Dz"],
-                       "K": cfg["K"], "S": cfg["S"], "parallelism": f"dp{world}",
-                       "l2": "inputs larger than L2 (x, z, dy = 192 MiB per rank)",
-                       "timing": "CUDA graph of one step replayed K times; CUDA events; max over ranks"},
+            "config": bench_config(cfg, world),
             "achieved_gbs": step_bytes / (ms_step * 1e-3) / 1e9,
             "step_hbm_frac": step_bytes / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"],
             "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
@@ -417,6 +428,7 @@ def main() -> None:
                          "traffic": traffic, "launch_ms": kernel_ms[dominant],
                          "algorithmic_bytes_per_launch": kbytes},
             "kernel_ms": kernel_ms,
+            "grad_allreduce_ms": allreduce_ms,
             "e2e": {"value": tokens_all / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
             "gpu_launches": launches_per_step * args.steps,

@@ -91,3 +91,4 @@ class GradAllReduce:
             g.copy_(self.flat[off:off + n].view_as(g))
             off += n
         return grads
+
