@@ -246,6 +246,136 @@ def cpu_baseline(cfg: dict, iters: int = 2, seq_tokens: int = 2048) -> dict:
             "sec_per_iter": t}
 
 
+DECODE = {"B": 128, "Dz": 4096, "K": 16, "S": 4, "prompt": 512,
+          "modules": (("q", 4096, "exp"), ("k", 1024, "exp"), ("v", 1024, "softmax"))}
+
+
+def decode_bytes_per_step(c: dict) -> int:
+    """Algorithmic HBM bytes of one decode step over all modules (bf16): per module x, z
+    and y rows, the S-1 cached states read and the S states written, basis and router W."""
+    total = 0
+    for _, D, _ in c["modules"]:
+        total += 2 * c["B"] * (D + c["Dz"] + D + (c["S"] - 1) * D + c["S"] * D)
+        total += 2 * c["K"] * c["S"] * D + 2 * c["K"] * c["Dz"]
+    return total
+
+
+def run_decode(args, rank: int, world: int, local_rank: int) -> None:
+    """Config 4: q / k / v MoC modules sharing z, caches prefilled from a 512-token prompt,
+    then one token per step for every sequence (replicas only for N > 1: each rank decodes
+    its own batch, no collective)."""
+    from moc import MoC, _lib
+    from moc.fused import decode_step
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:  # timing only: barrier and max over ranks
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
+    c = DECODE
+    torch.manual_seed(77)
+    mods, caches = [], []
+    g = torch.Generator().manual_seed(78 + rank)
+    with torch.no_grad():
+        z_p = torch.randn(c["B"], c["prompt"], c["Dz"], generator=g).bfloat16().to(device)
+        for name, D, ract in c["modules"]:
+            m = MoC(dim=D, z_dim=c["Dz"], kernel_size=c["S"], k=c["K"], init_std=0.002, router_activation=ract)
+            m.router.copy_(torch.randn(c["K"], c["Dz"], generator=g) * 0.02)
+            m = m.to(device=device, dtype=torch.bfloat16)
+            x_p = torch.randn(c["B"], c["prompt"], D, generator=g).bfloat16().to(device)
+            _, cache = m(x_p, z_p, output_final_state=True)
+            mods.append(m)
+            caches.append(cache.contiguous())
+            del x_p
+        del z_p
+        host_x = [torch.randn(c["B"], 1, D, generator=g).bfloat16() for _, D, _ in c["modules"]]
+        host_z = torch.randn(c["B"], 1, c["Dz"], generator=g).bfloat16()
+        xs = [h.to(device) for h in host_x]
+        z = host_z.to(device)
+
+        def step():  # one fused decode step: two launches for all modules
+            return decode_step(mods, xs, z, caches)
+
+        def step_per_module():  # MoC.step per module: router + update, six launches
+            return [m.step(x, z, cache)[0] for m, x, cache in zip(mods, xs, caches)]
+
+        for _ in range(args.warmup):
+            step_per_module()
+        g_pm = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_pm):
+            step_per_module()
+        for _ in range(args.warmup):
+            g_pm.replay()
+        ms_per_module = max_over_ranks(time_region(g_pm.replay, args.steps, torch.cuda.current_stream(device)),
+                                       world)
+        del g_pm
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        l0 = _lib.launch_count()
+        step()
+        torch.cuda.synchronize()
+        launches_per_step = _lib.launch_count() - l0
+        stream = torch.cuda.current_stream(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(args.warmup):
+            graph.replay()
+        sampler = ClockSampler(device, os.environ.get("TMPDIR", "/tmp"))
+        barrier(world)
+        t0 = time.time()
+        ms = time_region(graph.replay, args.steps, stream)
+        t1 = time.time()
+        barrier(world)
+        ms = max_over_ranks(ms, world)
+        clocks = sampler.summary(t0, t1)
+
+        pin_x = [h.pin_memory() for h in host_x]
+        pin_z = host_z.pin_memory()
+        outs = [torch.empty(c["B"], 1, D, dtype=torch.bfloat16).pin_memory() for _, D, _ in c["modules"]]
+
+        def e2e():
+            for d, h in zip(xs, pin_x):
+                d.copy_(h, non_blocking=True)
+            z.copy_(pin_z, non_blocking=True)
+            for o, y in zip(outs, step()):
+                o.copy_(y, non_blocking=True)
+
+        for _ in range(2):
+            e2e()
+        ms_e2e = max_over_ranks(time_region(e2e, max(3, min(args.steps, 50)), stream), world)
+    nbytes = decode_bytes_per_step(c)
+    peaks = measured_peaks()
+    if rank == 0:
+        us = ms * 1e3
+        print(json.dumps({
+            "metric": "MoC decode step latency (q, k, v modules)", "value": us, "unit": "us/step",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "config4: decode, q D=4096 / k D=1024 / v D=1024, z_dim=4096, K=16, S=4, "
+                                   "batch 128, caches prefilled from a 512-token prompt",
+                       "parallelism": f"replicas{world}",
+                       "timing": "CUDA graph of one fused decode step (all modules) replayed K times; CUDA events"},
+            "roofline": {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                         "algorithmic_bytes_per_step": nbytes,
+                         "bound_us": nbytes / (peaks["hbm_gbs"] * 1e9) * 1e6},
+            "e2e": {"value": ms_e2e * 1e3, "unit": "us/step",
+                    "h2d_bytes_per_step": sum(h.numel() * 2 for h in host_x) + host_z.numel() * 2,
+                    "d2h_bytes_per_step": sum(o.numel() * 2 for o in outs)},
+            "gpu_launches": launches_per_step * args.steps,
+            "per_module_path_us": ms_per_module * 1e3,
+            "clocks": clocks,
+        }), flush=True)
+    sampler.stop()
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def bench_config(cfg: dict, world: int) -> dict:
     """The workload description both arms print."""
     return {"workload": "config2: MoC module fwd+bwd, B=4 T=4096 D=z_dim=2048 K=16 S=4 bf16 softmax",
@@ -283,6 +413,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=("train", "decode"), default="train",
+                    help="train: config 2 (the headline); decode: config 4, three modules, batch 128")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -292,6 +424,9 @@ def main() -> None:
 
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.workload == "decode":
+        run_decode(args, rank, world, local_rank)
         return
 
     from moc import _lib, dp

@@ -187,6 +187,39 @@ int moc_prepare_chunk_indices(const void* cu_seqlens, int32_t cu_seqlens_dtype, 
                               int32_t chunk_size, int32_t* chunk_indices, int64_t n_chunks,
                               void* stream);
 
+/* One module of a fused multi-module decode step (MoC modules sharing the routing
+ * input z, as the q / k / v convolutions of an attention block do).  All pointers are
+ * bf16 device memory: router weight [n_bases, z_dim]; basis [n_bases, kernel_size, dim];
+ * x and out [batch, dim]; alpha [batch, n_bases] receives the router output; cache
+ * [batch, dim, kernel_size] contiguous, updated in place as in moc_step. */
+typedef struct moc_decode_module {
+  int64_t dim;
+  int32_t n_bases;            /* even, <= 16 */
+  int32_t kernel_size;        /* 1..4 */
+  int32_t activation;         /* 1 = fused SiLU */
+  int32_t router_act;         /* 0 = softmax, 1 = exp */
+  const void* weight;
+  const void* basis;
+  const void* x;
+  void* cache;
+  void* alpha;
+  void* out;
+} moc_decode_module;
+
+#define MOC_DECODE_MAX_MODULES 4
+
+/* Fused decode step of up to MOC_DECODE_MAX_MODULES modules that share z [batch, z_dim]:
+ * one launch computes every module's router (z read once per token tile), a second
+ * launch mixes and convolves every module's channels and shifts its cache.  Results
+ * equal moc_router_forward followed by moc_step for each module (bf16 products of
+ * alpha and basis summed in fp32, as the reference's bf16 decode).  dim must be even,
+ * z_dim a multiple of 8, pointers 16-byte aligned.  Replaces, per module, the router
+ * lines of MoC.forward (moc/api.py:383-388) and launch_update (moc/ops.py:341-362) with
+ * two launches for all modules (the fused multi-module decode of the reference's
+ * q / k / v usage, README.md:120-129). */
+int moc_decode_step_multi(int32_t n_modules, const moc_decode_module* modules, int64_t batch,
+                          int64_t z_dim, const void* z, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

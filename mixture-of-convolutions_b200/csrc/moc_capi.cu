@@ -173,6 +173,33 @@ int moc_step(int64_t batch, int64_t dim, int32_t n_bases, int32_t kernel_size, i
                    basis, cache, cache_strides, out, static_cast<cudaStream_t>(stream));
 }
 
+int moc_decode_step_multi(int32_t n_modules, const moc_decode_module* modules, int64_t batch, int64_t z_dim,
+                          const void* z, void* stream) {
+  if (n_modules < 1 || n_modules > MOC_DECODE_MAX_MODULES || !modules) return MOC_ERR_INVALID_ARGUMENT;
+  if (batch < 0 || z_dim <= 0) return MOC_ERR_INVALID_ARGUMENT;
+  if (z_dim % 8 != 0 || batch > (int64_t{1} << 30) || z_dim > (int64_t{1} << 40)) return MOC_ERR_UNSUPPORTED_SHAPE;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const int32_t S = modules[0].kernel_size;
+  int64_t blocks = 0;
+  for (int i = 0; i < n_modules; ++i) {
+    const moc_decode_module& m = modules[i];
+    if (m.dim <= 0 || m.n_bases <= 0 || m.kernel_size <= 0) return MOC_ERR_INVALID_ARGUMENT;
+    if ((m.activation != 0 && m.activation != 1) || (m.router_act != 0 && m.router_act != 1))
+      return MOC_ERR_INVALID_ARGUMENT;
+    if (m.n_bases > 16 || m.kernel_size > 4 || m.kernel_size != S || m.dim % 2 != 0 || m.dim > (int64_t{1} << 40))
+      return MOC_ERR_UNSUPPORTED_SHAPE;
+    if (!m.weight || !m.basis || !m.x || !m.cache || !m.alpha || !m.out) return MOC_ERR_INVALID_ARGUMENT;
+    if (!a16(m.weight) || !a16(m.basis) || !a16(m.x) || !a16(m.cache) || !a16(m.alpha) || !a16(m.out))
+      return MOC_ERR_MISALIGNED;
+    blocks += (m.dim + 255) / 256;
+  }
+  if (blocks > (int64_t{1} << 30)) return MOC_ERR_UNSUPPORTED_SHAPE;
+  if (batch == 0) return MOC_OK;
+  if (!z) return MOC_ERR_INVALID_ARGUMENT;
+  if (!a16(z)) return MOC_ERR_MISALIGNED;
+  return decode_step_multi(n_modules, modules, batch, z_dim, z, static_cast<cudaStream_t>(stream));
+}
+
 int moc_router_forward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t dtype, int32_t router_act,
                        const void* z, const void* weight, void* alpha, void* stream) {
   if (!valid_float_dtype(dtype)) return MOC_ERR_UNSUPPORTED_DTYPE;

@@ -50,6 +50,9 @@ int tc_router_backward(int64_t N, int64_t Dz, int K, int act, const void* z, con
 int tc_router_backward_noalloc(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, const void* alpha,
                                const void* dalpha, int da_dtype, void* dz, void* dw, cudaStream_t st);
 
+// fused decode step of up to MOC_DECODE_MAX_MODULES modules sharing z (moc_decode.cu)
+int decode_step_multi(int n, const moc_decode_module* mods, int64_t B, int64_t Dz, const void* z, cudaStream_t st);
+
 // device status words of the TMA-staged kernels (bounded-wait timeouts), read/cleared
 // by moc_device_status(); and a probe kernel that exercises the timeout path.
 int router_status(int* out, bool clear);

@@ -46,6 +46,26 @@ class MocProblem(ctypes.Structure):
     ]
 
 
+class MocDecodeModule(ctypes.Structure):
+    """Mirror of ``struct moc_decode_module``."""
+
+    _fields_ = [
+        ("dim", ctypes.c_int64),
+        ("n_bases", ctypes.c_int32),
+        ("kernel_size", ctypes.c_int32),
+        ("activation", ctypes.c_int32),
+        ("router_act", ctypes.c_int32),
+        ("weight", ctypes.c_void_p),
+        ("basis", ctypes.c_void_p),
+        ("x", ctypes.c_void_p),
+        ("cache", ctypes.c_void_p),
+        ("alpha", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+    ]
+
+
+DECODE_MAX_MODULES = 4
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int32
@@ -79,6 +99,7 @@ SIGNATURES = {
         [_I64, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _P, _P, _P],
     ),
     "moc_prepare_chunk_indices": (ctypes.c_int, [_P, _I32, _I64, _I32, _P, _I64, _P]),
+    "moc_decode_step_multi": (ctypes.c_int, [_I32, ctypes.POINTER(MocDecodeModule), _I64, _I64, _P, _P]),
 }
 
 _lib = None

@@ -1,0 +1,111 @@
+"""Fused decode step for MoC modules that share their routing input.
+
+In the reference's attention block (README.md:120-129) the q, k and v short convolutions
+are three MoC modules routed by the same ``x_norm``.  Decoding one token through them one
+by one costs, per module, a router GEMM, its softmax / exp and the update kernel
+(moc/api.py:383-388, moc/ops.py:341-362).  ``decode_step`` runs all of them in two
+launches of ``moc_decode_step_multi``: one computes every module's router from one pass
+over z, the other mixes, convolves and shifts every module's cache.
+
+Results match calling ``module.step(x, z, cache)`` for each module; shapes the fused
+kernels do not cover (fp32 or fp16 modules, more than 16 bases, kernel sizes above 4,
+mixed kernel sizes, more than four modules) take that per-module path.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Sequence
+
+import torch
+
+from . import _lib
+from .api import MoC
+
+_ROUTER_ACTS = {"softmax": 0, "exp": 1}
+
+
+def _as_2d(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.ndim == 3:
+        if t.shape[1] != 1:
+            raise ValueError(f"{name} must have one token per sequence, got shape {tuple(t.shape)}")
+        return t[:, 0]
+    if t.ndim != 2:
+        raise ValueError(f"{name} must be [B, 1, D] or [B, D], got shape {tuple(t.shape)}")
+    return t
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+def _fusable(modules: Sequence[MoC], xs, z, caches) -> bool:
+    if not 1 <= len(modules) <= _lib.DECODE_MAX_MODULES:
+        return False
+    S = modules[0].kernel_size
+    for m, x, c in zip(modules, xs, caches):
+        if m.conv_bases.dtype != torch.bfloat16 or m.router.dtype != torch.bfloat16:
+            return False
+        if x.dtype != torch.bfloat16 or c.dtype != torch.bfloat16 or not c.is_contiguous():
+            return False
+        if m.k > 16 or m.kernel_size != S or S > 4 or m.dim % 2 != 0:
+            return False
+        if c.data_ptr() % 16 != 0:
+            return False
+    return z.dtype == torch.bfloat16 and z.shape[-1] % 8 == 0
+
+
+def decode_step(modules: Sequence[MoC], xs: Sequence[torch.Tensor], z: torch.Tensor,
+                caches: Sequence[torch.Tensor]) -> list[torch.Tensor]:
+    """One decode token through every module in ``modules``.
+
+    modules: MoC modules with the same z_dim, on one CUDA device.
+    xs:      per module, the token's input [B, 1, D_i] (or [B, D_i]).
+    z:       the shared routing input [B, 1, z_dim] (or [B, z_dim]).
+    caches:  per module, its conv cache [B, D_i, kernel_size]; updated in place, as
+             ``MoC.step`` does (slots shift left, x enters the last slot).
+
+    Returns the outputs y_i, shaped like xs[i]."""
+    if not (len(modules) == len(xs) == len(caches)) or not modules:
+        raise ValueError("decode_step needs one x and one cache per module")
+    z2 = _as_2d(z, "z")
+    x2 = [_as_2d(x, "x") for x in xs]
+    B = z2.shape[0]
+    for m, x, c in zip(modules, x2, caches):
+        if not isinstance(m, MoC):
+            raise TypeError("decode_step expects moc.MoC modules")
+        if x.shape != (B, m.dim):
+            raise ValueError(f"x must be [B, {m.dim}] for this module, got {tuple(x.shape)}")
+        if c.shape != (B, m.dim, m.kernel_size):
+            raise ValueError(f"cache must be [B, {m.dim}, {m.kernel_size}], got {tuple(c.shape)}")
+        if z2.shape[1] != m.z_dim:
+            raise ValueError(f"z must have z_dim={m.z_dim}, got {z2.shape[1]}")
+        if not (x.is_cuda and c.is_cuda and z2.is_cuda and m.conv_bases.is_cuda):
+            raise ValueError("decode_step runs on CUDA tensors")
+    if not _fusable(modules, x2, z2, caches):
+        zs = z2.unsqueeze(1)
+        return [m.step(x.unsqueeze(1), zs, c)[0].reshape(xo.shape)
+                for m, x, c, xo in zip(modules, x2, caches, xs)]
+
+    z2 = _aligned(z2)
+    keep = [z2]
+    mods = (_lib.MocDecodeModule * len(modules))()
+    ys, alphas = [], []
+    for i, (m, x, c) in enumerate(zip(modules, x2, caches)):
+        x = _aligned(x)
+        w = _aligned(m.router.detach())
+        b = _aligned(m.conv_bases.detach())
+        y = torch.empty_like(x)
+        alpha = torch.empty(B, m.k, dtype=torch.bfloat16, device=x.device)
+        keep += [x, w, b]
+        ys.append(y)
+        alphas.append(alpha)
+        mods[i] = _lib.MocDecodeModule(
+            dim=m.dim, n_bases=m.k, kernel_size=m.kernel_size, activation=int(m.activation is not None),
+            router_act=_ROUTER_ACTS[m.router_activation], weight=w.data_ptr(), basis=b.data_ptr(),
+            x=x.data_ptr(), cache=c.data_ptr(), alpha=alpha.data_ptr(), out=y.data_ptr())
+    with torch.cuda.device(z2.device):
+        rc = _lib.load().moc_decode_step_multi(len(modules), mods, B, z2.shape[1], z2.data_ptr(),
+                                               _lib.stream_of(z2.device))
+    _lib.check(rc, "moc_decode_step_multi")
+    return [y.reshape(xo.shape) for y, xo in zip(ys, xs)]

@@ -102,3 +102,61 @@ def test_step_router_and_chunk_checks():
     assert lib.moc_router_forward(4, 8, 4, 2, 3, 1, 1, 1, None) == 1
     assert lib.moc_prepare_chunk_indices(1, 0, 1, 0, 1, 1, None) == 1
     assert lib.moc_set_kernel_path(5) == 1
+
+
+def _c_layout(struct: str, fields: list[str]) -> dict[str, int]:
+    """sizeof / offsetof of a header struct, compiled with the host C compiler."""
+    import shutil
+    import subprocess
+    import tempfile
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no host C compiler")
+    body = "".join(f'printf("{f} %zu\\n", offsetof({struct}, {f}));' for f in fields)
+    src = (f'#include <stddef.h>\n#include <stdio.h>\n#include "{HEADER}"\n'
+           f'int main(void) {{ printf("sizeof %zu\\n", sizeof({struct})); {body} return 0; }}\n')
+    with tempfile.TemporaryDirectory() as d:
+        with open(os.path.join(d, "l.c"), "w") as f:
+            f.write(src)
+        exe = os.path.join(d, "l")
+        subprocess.run([cc, "-I", os.path.join(ROOT, "include"), os.path.join(d, "l.c"), "-o", exe], check=True)
+        out = subprocess.run([exe], check=True, capture_output=True, text=True).stdout
+    return {k: int(v) for k, v in (line.split() for line in out.splitlines())}
+
+
+@pytest.mark.parametrize("struct,mirror", [("moc_problem", _lib.MocProblem),
+                                           ("moc_decode_module", _lib.MocDecodeModule)])
+def test_ctypes_structs_match_the_header_layout(struct, mirror):
+    names = [f[0] for f in mirror._fields_]
+    layout = _c_layout(struct, names)
+    assert layout["sizeof"] == ctypes.sizeof(mirror)
+    for n in names:
+        assert layout[n] == getattr(mirror, n).offset, n
+
+
+def test_decode_multi_checks():
+    lib = _lib.load()
+
+    def mods(n, **kw):
+        arr = (_lib.MocDecodeModule * n)()
+        for i in range(n):
+            f = dict(dim=64, n_bases=16, kernel_size=4, activation=0, router_act=0, weight=256, basis=512,
+                     x=768, cache=1024, alpha=1280, out=1536)
+            f.update(kw)
+            arr[i] = _lib.MocDecodeModule(**f)
+        return arr
+
+    assert lib.moc_decode_step_multi(0, mods(1), 4, 64, 2048, None) == 1
+    assert lib.moc_decode_step_multi(5, mods(5), 4, 64, 2048, None) == 1
+    assert lib.moc_decode_step_multi(1, mods(1, n_bases=17), 4, 64, 2048, None) == 3
+    assert lib.moc_decode_step_multi(1, mods(1, kernel_size=5), 4, 64, 2048, None) == 3
+    assert lib.moc_decode_step_multi(1, mods(1, dim=63), 4, 64, 2048, None) == 3
+    assert lib.moc_decode_step_multi(1, mods(1), 4, 60, 2048, None) == 3  # z_dim % 8
+    assert lib.moc_decode_step_multi(1, mods(1, router_act=2), 4, 64, 2048, None) == 1
+    assert lib.moc_decode_step_multi(1, mods(1, cache=1030), 4, 64, 2048, None) == 4
+    assert lib.moc_decode_step_multi(1, mods(1, x=0), 4, 64, 2048, None) == 1
+    two = mods(2)
+    two[1].kernel_size = 2
+    assert lib.moc_decode_step_multi(2, two, 4, 64, 2048, None) == 3  # one kernel size for all modules
+    assert lib.moc_decode_step_multi(2, mods(2), 0, 64, 2048, None) == 0  # empty batch: no work

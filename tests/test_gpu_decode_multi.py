@@ -1,0 +1,100 @@
+"""Fused multi-module decode (moc.fused.decode_step / moc_decode_step_multi) against the
+per-module path (MoC.step, i.e. router + moc_step) and the float64 oracle.
+
+Modules sharing z, with caches prefilled from a prompt, decode several tokens.  Per step:
+* the caches are bitwise equal to the per-module path's (they only move stored values);
+* y agrees with the per-module path within 2e-2 of max|y| (both form bf16 alpha*basis
+  products and sum them in fp32; the router logits are summed in another order);
+* y agrees within 2e-2 with the oracle step (bf16 products, float64 sums) fed the float64
+  router's alpha rounded to bf16, and the oracle's new cache is bitwise the fused one.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import rel_err
+from moc import MoC, _lib
+from moc.fused import decode_step
+from oracle import moc_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+
+
+def _modules(specs, z_dim, ks, seed):
+    torch.manual_seed(seed)
+    mods = []
+    g = torch.Generator().manual_seed(seed + 1)
+    for dim, k, ract, act in specs:
+        m = MoC(dim=dim, z_dim=z_dim, kernel_size=ks, k=k, init_std=0.05, router_activation=ract,
+                activation=act)
+        with torch.no_grad():
+            m.router.copy_(torch.randn(k, z_dim, generator=g) * 0.05)
+        mods.append(m.cuda().bfloat16())
+    return mods
+
+
+def _run(specs, B, z_dim, ks, steps=4, prompt=9, seed=3):
+    mods = _modules(specs, z_dim, ks, seed)
+    g = torch.Generator().manual_seed(seed + 2)
+    zp = torch.randn(B, prompt, z_dim, generator=g).bfloat16().cuda()
+    caches = []
+    with torch.no_grad():
+        for m in mods:
+            xp = torch.randn(B, prompt, m.dim, generator=g).bfloat16().cuda()
+            caches.append(m(xp, zp, output_final_state=True)[1].contiguous())
+        ref_caches = [c.clone() for c in caches]
+        for _ in range(steps):
+            z = torch.randn(B, 1, z_dim, generator=g).bfloat16().cuda()
+            xs = [torch.randn(B, 1, m.dim, generator=g).bfloat16().cuda() for m in mods]
+            before = [c.clone() for c in caches]
+            ys = decode_step(mods, xs, z, caches)
+            refs = [m.step(x, z, c)[0] for m, x, c in zip(mods, xs, ref_caches)]
+            for i, (m, x, y, r) in enumerate(zip(mods, xs, ys, refs)):
+                assert y.shape == x.shape
+                assert torch.equal(caches[i], ref_caches[i]), f"module {i}: cache differs"
+                assert rel_err(y, r) <= TOL, f"module {i}: {rel_err(y, r):.3e}"
+                # the oracle on the same inputs
+                a64 = O.router(z[:, 0].double().cpu(), m.router.detach().double().cpu(), m.router_activation)
+                yo, so = O.step(x[:, 0].double().cpu(), a64.bfloat16().double(),
+                                m.conv_bases.detach().double().cpu(), before[i].double().cpu(),
+                                m.activation, bf16_products=True)
+                assert rel_err(y[:, 0], yo) <= TOL
+                assert torch.equal(caches[i].double().cpu(), so)
+
+
+def test_qkv_shaped_modules():
+    # q / k / v as in the reference's attention block: exp, exp, softmax routers
+    _run([(512, 16, "exp", None), (128, 16, "exp", None), (128, 16, "softmax", None)], B=37, z_dim=256, ks=4)
+
+
+@pytest.mark.parametrize("ks", [1, 2, 3, 4])
+def test_kernel_sizes_bases_and_silu(ks):
+    _run([(96, 8, "softmax", "silu"), (258, 16, "exp", None)], B=5, z_dim=520, ks=ks, seed=ks)
+
+
+def test_single_module_and_single_sequence():
+    _run([(64, 4, "softmax", None)], B=1, z_dim=64, ks=4, steps=3)
+
+
+def test_four_modules_and_large_batch():
+    _run([(256, 16, "softmax", None)] * 4, B=130, z_dim=128, ks=4, steps=2)
+
+
+def test_unfusable_modules_take_the_per_module_path():
+    # more than 16 bases: decode_step falls back to MoC.step and still agrees
+    _run([(64, 32, "softmax", None), (64, 16, "exp", None)], B=3, z_dim=64, ks=4, steps=2)
+
+
+def test_fused_path_is_two_launches():
+    mods = _modules([(512, 16, "exp", None), (128, 16, "exp", None), (128, 16, "softmax", None)], 256, 4, 9)
+    B = 8
+    caches = [torch.zeros(B, m.dim, 4, dtype=torch.bfloat16, device="cuda") for m in mods]
+    xs = [torch.randn(B, 1, m.dim, device="cuda").bfloat16() for m in mods]
+    z = torch.randn(B, 1, 256, device="cuda").bfloat16()
+    n0 = _lib.launch_count()
+    decode_step(mods, xs, z, caches)
+    torch.cuda.synchronize()
+    assert _lib.launch_count() - n0 == 2
