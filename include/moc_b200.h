@@ -194,7 +194,7 @@ int moc_prepare_chunk_indices(const void* cu_seqlens, int32_t cu_seqlens_dtype, 
  * [batch, dim, kernel_size] contiguous, updated in place as in moc_step. */
 typedef struct moc_decode_module {
   int64_t dim;
-  int32_t n_bases;            /* even, <= 16 */
+  int32_t n_bases;            /* <= 16 */
   int32_t kernel_size;        /* 1..4 */
   int32_t activation;         /* 1 = fused SiLU */
   int32_t router_act;         /* 0 = softmax, 1 = exp */
@@ -211,9 +211,10 @@ typedef struct moc_decode_module {
 /* Fused decode step of up to MOC_DECODE_MAX_MODULES modules that share z [batch, z_dim]:
  * one launch computes every module's router (z read once per token tile), a second
  * launch mixes and convolves every module's channels and shifts its cache.  Results
- * equal moc_router_forward followed by moc_step for each module (bf16 products of
- * alpha and basis summed in fp32, as the reference's bf16 decode).  dim must be even,
- * z_dim a multiple of 8, pointers 16-byte aligned.  Replaces, per module, the router
+ * agree with moc_router_forward followed by moc_step for each module within the bf16
+ * tolerance: here the alpha.basis products enter an fp32 tensor-core sum exactly, where
+ * moc_step (like the reference's decode kernel) rounds each product to bf16.  All modules share
+ * one kernel_size; z_dim must be a multiple of 8 and every pointer 16-byte aligned.  Replaces, per module, the router
  * lines of MoC.forward (moc/api.py:383-388) and launch_update (moc/ops.py:341-362) with
  * two launches for all modules (the fused multi-module decode of the reference's
  * q / k / v usage, README.md:120-129). */

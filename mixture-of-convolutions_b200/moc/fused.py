@@ -48,7 +48,7 @@ def _fusable(modules: Sequence[MoC], xs, z, caches) -> bool:
             return False
         if x.dtype != torch.bfloat16 or c.dtype != torch.bfloat16 or not c.is_contiguous():
             return False
-        if m.k > 16 or m.kernel_size != S or S > 4 or m.dim % 2 != 0:
+        if m.k > 16 or m.kernel_size != S or S > 4:
             return False
         if c.data_ptr() % 16 != 0:
             return False

@@ -3,8 +3,9 @@ per-module path (MoC.step, i.e. router + moc_step) and the float64 oracle.
 
 Modules sharing z, with caches prefilled from a prompt, decode several tokens.  Per step:
 * the caches are bitwise equal to the per-module path's (they only move stored values);
-* y agrees with the per-module path within 2e-2 of max|y| (both form bf16 alpha*basis
-  products and sum them in fp32; the router logits are summed in another order);
+* y agrees with the per-module path within 2e-2 of max|y| (that path rounds each
+  alpha*basis product to bf16 like the reference's decode kernel; the fused one sums the
+  exact products in fp32 on the tensor cores, and sums the router logits in another order);
 * y agrees within 2e-2 with the oracle step (bf16 products, float64 sums) fed the float64
   router's alpha rounded to bf16, and the oracle's new cache is bitwise the fused one.
 """
@@ -72,7 +73,8 @@ def test_qkv_shaped_modules():
 
 @pytest.mark.parametrize("ks", [1, 2, 3, 4])
 def test_kernel_sizes_bases_and_silu(ks):
-    _run([(96, 8, "softmax", "silu"), (258, 16, "exp", None)], B=5, z_dim=520, ks=ks, seed=ks)
+    _run([(96, 8, "softmax", "silu"), (258, 16, "exp", None), (37, 5, "exp", "silu")], B=5, z_dim=520, ks=ks,
+         seed=ks)
 
 
 def test_single_module_and_single_sequence():
@@ -81,6 +83,11 @@ def test_single_module_and_single_sequence():
 
 def test_four_modules_and_large_batch():
     _run([(256, 16, "softmax", None)] * 4, B=130, z_dim=128, ks=4, steps=2)
+
+
+def test_long_routing_input():
+    # z_dim spans more chunks than the router cluster has CTAs
+    _run([(128, 16, "softmax", None), (64, 16, "exp", None)], B=20, z_dim=8200, ks=4, steps=2)
 
 
 def test_unfusable_modules_take_the_per_module_path():
