@@ -180,15 +180,15 @@ __global__ void k_wait_timeout_probe(uint32_t limit) {
 template <int KT>
 struct BwdLayout {
   static constexpr int KP = KT * 16;
-  static constexpr int DLB = (KP + 8) * 2;  // dl row bytes
+  static constexpr int DLB = (KP + 8) * 2;       // dl row bytes (padded, conflict-free ldmatrix)
+  static constexpr int zbox = kBwdTile * 128;    // one 64-token x 64-column box, 128 B rows (swizzled)
+  static constexpr int z_bytes = 2 * zbox;       // 128 columns
   static constexpr int w_bytes = KP * kRowB;
-  static constexpr int z_bytes = kBwdTile * kRowB;
-  static constexpr int dl_bytes = kBwdTile * DLB;
-  static constexpr int total = w_bytes + 2 * z_bytes + dl_bytes;
+  static constexpr int dl_bytes = kBwdTile * DLB;  // one of two dl buffers
+  static constexpr int total = 1024 + 2 * z_bytes + w_bytes + 2 * dl_bytes + 64;
 };
 
 struct RouterBwdArgs {
-  const bf16* z;
   const bf16* w;
   const bf16* alpha;
   const void* dalpha;
@@ -200,14 +200,19 @@ struct RouterBwdArgs {
   int64_t tiles_per_group;
 };
 
+// TMA-staged backward: thread 0 double-buffers 64-token x 128-column z tiles (two
+// 128B-swizzled boxes) on mbarriers; every thread computes dlogits for the next tile's
+// tokens meanwhile.
 template <int KT>
-__global__ void __launch_bounds__(256) k_router_bwd_tc(RouterBwdArgs a) {
+__global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ CUtensorMap zmap, RouterBwdArgs a) {
   using L = BwdLayout<KT>;
   constexpr int KP = L::KP;
-  extern __shared__ __align__(128) char smem[];
-  char* w_s = smem;
-  char* z_st = smem + L::w_bytes;
-  char* dl_s = z_st + 2 * L::z_bytes;
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t z_st = smem_addr(smem);
+  char* w_s = smem + 2 * L::z_bytes;
+  char* dl_s = w_s + L::w_bytes;
+  const uint32_t bar0 = smem_addr(dl_s + 2 * L::dl_bytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int64_t col_base = static_cast<int64_t>(blockIdx.x) * kZC;
@@ -217,102 +222,133 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(RouterBwdArgs a) {
   const int cw = warp * 16;  // this warp's 16 columns inside the slice
   const bool want_dz = a.dz != nullptr;
   const bool want_dw = a.dw_part != nullptr;
+  // zT ldmatrix: rows (lane&7) + (lane>>4)*8, 16-byte chunk 2*(warp&3) + ((lane>>3)&1) of box warp>>2
+  const uint32_t zt_box = static_cast<uint32_t>((warp >> 2) * L::zbox);
+  const int zt_row = (lane & 7) + (lane >> 4) * 8;
+  const int zt_chunk = 2 * (warp & 3) + ((lane >> 3) & 1);
 
-  auto load_z = [&](int64_t tile, char* dst) {
-    for (int idx = threadIdx.x; idx < kBwdTile * 16; idx += 256) {
-      const int row = idx >> 4, chunk = idx & 15;
-      const int64_t tok = tile * kBwdTile + row;
-      const int64_t col = col_base + chunk * 8;
-      const bool ok = tok < a.N && col < a.Dz;
-      cp_async16(smem_addr(dst + row * kRowB + chunk * 16), ok ? a.z + tok * a.Dz + col : a.z, ok ? 16u : 0u);
-    }
+  auto issue = [&](int64_t tile, int stage) {
+    const uint32_t bar = bar0 + 8 * stage;
+    const uint32_t dst = z_st + stage * L::z_bytes;
+    fence_proxy_async();
+    mbar_expect_tx(bar, L::z_bytes);
+    tma_load_2d(dst, &zmap, static_cast<int>(col_base), static_cast<int>(tile * kBwdTile), bar);
+    tma_load_2d(dst + L::zbox, &zmap, static_cast<int>(col_base) + 64, static_cast<int>(tile * kBwdTile), bar);
   };
 
   float dwa[2 * KT][4] = {};  // dW^T: (column cw + g | +8) x (base 8kn + 2q..)
+  uint32_t wb[KT][4];         // W as the B operand of dz = dl . W (this warp's 16 columns)
   if (i0 < i1) {
+    if (threadIdx.x == 0) {
+      tma_prefetch_desc(&zmap);
+      mbar_init(bar0, 1);
+      mbar_init(bar0 + 8, 1);
+      fence_mbar_init();
+    }
     for (int idx = threadIdx.x; idx < KP * 16; idx += 256) {
       const int k = idx >> 4, chunk = idx & 15;
       const int64_t col = col_base + chunk * 8;
       const bool ok = k < a.K && col < a.Dz;
       cp_async16(smem_addr(w_s + k * kRowB + chunk * 16), ok ? a.w + k * a.Dz + col : a.w, ok ? 16u : 0u);
     }
-    load_z(i0, z_st);
     cp_async_commit();
+    __syncthreads();
+    if (threadIdx.x == 0) issue(i0, 0);
+    cp_async_wait<0>();
+    __syncthreads();
+#pragma unroll
+    for (int kt = 0; kt < KT; ++kt)
+      ldsm_x4_t(smem_addr(w_s + (kt * 16 + lm_row(lane)) * kRowB + (cw + lm_col(lane)) * 2), wb[kt]);
   }
+  // alpha / dalpha of the next tile are loaded one iteration ahead into registers: four
+  // threads per token, each owning KP/4 bases
+  constexpr int KQ = KP / 4;
+  const int dl_row = threadIdx.x >> 2, dl_part = threadIdx.x & 3;
+  float av[KQ], dv[KQ];
+  auto fetch = [&](int64_t tile) {
+    const int64_t tok = tile * kBwdTile + dl_row;
+#pragma unroll
+    for (int e = 0; e < KQ; ++e) {
+      const int k = dl_part * KQ + e;
+      const bool ok = tok < a.N && k < a.K;
+      av[e] = ok ? __bfloat162float(a.alpha[tok * a.K + k]) : 0.f;
+      dv[e] = ok ? ld_any(a.dalpha, a.da_dtype, tok * a.K + k) : 0.f;
+    }
+  };
+  if (i0 < i1) fetch(i0);
+
   for (int64_t it = i0; it < i1; ++it) {
     const int cur = static_cast<int>((it - i0) & 1);
-    // dlogits for this tile's 64 tokens (bf16, like the reference's bf16 autograd): four
-    // threads per token, each owning KP/4 bases; the softmax dot is a quad reduction.
+    const uint32_t parity = static_cast<uint32_t>(((it - i0) >> 1) & 1);
+    char* dl_cur = dl_s + cur * L::dl_bytes;  // tile it-2 used it; its readers passed the last wait barrier
+    // dlogits for this tile's 64 tokens (bf16, like the reference's bf16 autograd); the
+    // softmax dot is a quad reduction.
     {
-      constexpr int KQ = KP / 4;
-      const int row = threadIdx.x >> 2, part = threadIdx.x & 3;
-      const int64_t tok = it * kBwdTile + row;
-      float av[KQ], dv[KQ];
       float dot = 0.f;
 #pragma unroll
-      for (int e = 0; e < KQ; ++e) {
-        const int k = part * KQ + e;
-        const bool ok = tok < a.N && k < a.K;
-        av[e] = ok ? __bfloat162float(a.alpha[tok * a.K + k]) : 0.f;
-        dv[e] = ok ? ld_any(a.dalpha, a.da_dtype, tok * a.K + k) : 0.f;
-        dot = fmaf(av[e], dv[e], dot);
-      }
+      for (int e = 0; e < KQ; ++e) dot = fmaf(av[e], dv[e], dot);
       dot += __shfl_xor_sync(0xffffffffu, dot, 1);
       dot += __shfl_xor_sync(0xffffffffu, dot, 2);
       if (a.act != 0) dot = 0.f;
-      bf16* dst = reinterpret_cast<bf16*>(dl_s + row * L::DLB) + part * KQ;
+      bf16* dst = reinterpret_cast<bf16*>(dl_cur + dl_row * L::DLB) + dl_part * KQ;
 #pragma unroll
       for (int e = 0; e < KQ; ++e) dst[e] = __float2bfloat16_rn(av[e] * (dv[e] - dot));
     }
-    if (it + 1 < i1) {
-      load_z(it + 1, z_st + (cur ^ 1) * L::z_bytes);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+    if (it + 1 < i1) fetch(it + 1);
+    const bool landed = mbar_wait(bar0 + 8 * cur, parity);
+    if (__syncthreads_or(!landed)) {
+      if (threadIdx.x == 0) {
+        atomicOr(&g_router_status, kStatusWaitTimeout);
+        mbar_wait(bar0 + 8 * cur, parity);
+      }
+      return;
     }
-    __syncthreads();
-    const char* z_s = z_st + cur * L::z_bytes;
+    // every thread is past tile it-1, so its stage can be refilled with tile it+1
+    if (threadIdx.x == 0 && it + 1 < i1) issue(it + 1, cur ^ 1);
+    const uint32_t z_s = z_st + cur * L::z_bytes;
     const int64_t tok0 = it * kBwdTile;
     for (int b = 0; b < kBwdTile / 16; ++b) {
       if (tok0 + 16 * b >= a.N) break;
+      uint32_t af[KT][4];  // dl rows of this block (A operand of dz)
+#pragma unroll
+      for (int kt = 0; kt < KT; ++kt)
+        ldsm_x4(smem_addr(dl_cur + (16 * b + lm_row(lane)) * L::DLB + (kt * 16 + lm_col(lane)) * 2), af[kt]);
       if (want_dz) {
         // dz[tok, col] = sum_k dl[tok, k] W[k, col]
-        float acc[2][4] = {};
+        float acc[2][4];
+        mma_bf16_z(acc[0], af[0], wb[0][0], wb[0][1]);
+        mma_bf16_z(acc[1], af[0], wb[0][2], wb[0][3]);
 #pragma unroll
-        for (int kt = 0; kt < KT; ++kt) {
-          uint32_t af[4], bf[4];
-          ldsm_x4(smem_addr(dl_s + (16 * b + lm_row(lane)) * L::DLB + (kt * 16 + lm_col(lane)) * 2), af);
-          ldsm_x4_t(smem_addr(w_s + (kt * 16 + lm_row(lane)) * kRowB + (cw + lm_col(lane)) * 2), bf);
-          mma_bf16(acc[0], af, bf[0], bf[1]);
-          mma_bf16(acc[1], af, bf[2], bf[3]);
+        for (int kt = 1; kt < KT; ++kt) {
+          mma_bf16(acc[0], af[kt], wb[kt][0], wb[kt][1]);
+          mma_bf16(acc[1], af[kt], wb[kt][2], wb[kt][3]);
         }
+        bf16* dz_row = a.dz + (tok0 + 16 * b + g) * a.Dz + col_base + cw + 2 * q;
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int64_t col = col_base + cw + nt * 8 + 2 * q;
+        for (int h = 0; h < 2; ++h) {
+          if (tok0 + 16 * b + g + 8 * h < a.N) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int64_t tok = tok0 + 16 * b + g + 8 * h;
-            if (tok < a.N && col < a.Dz)
-              *reinterpret_cast<uint32_t*>(a.dz + tok * a.Dz + col) = pack_bf16(acc[nt][2 * h], acc[nt][2 * h + 1]);
+            for (int nt = 0; nt < 2; ++nt)
+              if (col_base + cw + nt * 8 < a.Dz)
+                *reinterpret_cast<uint32_t*>(dz_row + 8 * h * a.Dz + nt * 8) =
+                    pack_bf16(acc[nt][2 * h], acc[nt][2 * h + 1]);
           }
         }
       }
       if (want_dw) {
         // dW^T[col, k] += sum_tok z[tok, col] dl[tok, k]
         uint32_t zt[4];
-        ldsm_x4_t(smem_addr(z_s + (16 * b + (lane & 7) + (lane >> 4) * 8) * kRowB + (cw + ((lane >> 3) & 1) * 8) * 2),
-                  zt);
+        const int r = 16 * b + zt_row;
+        ldsm_x4_t(z_s + zt_box + r * 128 + (((zt_chunk ^ r) & 7) << 4), zt);
 #pragma unroll
         for (int kt = 0; kt < KT; ++kt) {
           uint32_t db[4];
-          ldsm_x4_t(smem_addr(dl_s + (16 * b + lm_row(lane)) * L::DLB + (kt * 16 + lm_col(lane)) * 2), db);
+          ldsm_x4_t(smem_addr(dl_cur + (16 * b + lm_row(lane)) * L::DLB + (kt * 16 + lm_col(lane)) * 2), db);
           mma_bf16(dwa[2 * kt], zt, db[0], db[1]);
           mma_bf16(dwa[2 * kt + 1], zt, db[2], db[3]);
         }
       }
     }
-    __syncthreads();
   }
   if (want_dw) {
     const int64_t grp = blockIdx.y;
@@ -385,12 +421,16 @@ int fwd_kt(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, 
 }
 
 template <int KT>
-int bwd_kt(RouterBwdArgs& a, int64_t slices, int64_t groups, void* dw, cudaStream_t st) {
+int bwd_kt(RouterBwdArgs& a, const void* z, int64_t slices, int64_t groups, void* dw, cudaStream_t st) {
   static bool configured[64] = {};
   int rc = set_smem(reinterpret_cast<const void*>(k_router_bwd_tc<KT>), configured, BwdLayout<KT>::total);
   if (rc != MOC_OK) return rc;
+  CUtensorMap zmap;
+  rc = make_tmap_bf16_2d(&zmap, z, static_cast<uint64_t>(a.Dz), static_cast<uint64_t>(a.N),
+                         static_cast<uint64_t>(a.Dz) * 2, 64, kBwdTile);
+  if (rc != MOC_OK) return rc;
   k_router_bwd_tc<KT><<<dim3(static_cast<unsigned>(slices), static_cast<unsigned>(groups)), 256,
-                        BwdLayout<KT>::total, st>>>(a);
+                        BwdLayout<KT>::total, st>>>(zmap, a);
   note_launch();
   if (dw != nullptr) {
     const int64_t n = static_cast<int64_t>(a.K) * a.Dz;
@@ -426,7 +466,6 @@ int tc_router_backward(int64_t N, int64_t Dz, int K, int act, const void* z, con
   if (ws_bytes < tc_router_backward_ws(N, Dz, K)) return MOC_ERR_WORKSPACE_TOO_SMALL;
   if (dz == nullptr && dw == nullptr) return MOC_OK;
   RouterBwdArgs a{};
-  a.z = static_cast<const bf16*>(z);
   a.w = static_cast<const bf16*>(w);
   a.alpha = static_cast<const bf16*>(alpha);
   a.dalpha = dalpha;
@@ -440,7 +479,7 @@ int tc_router_backward(int64_t N, int64_t Dz, int K, int act, const void* z, con
   int64_t slices, groups, tpg;
   bwd_plan(N, Dz, slices, groups, tpg);
   a.tiles_per_group = tpg;
-  return K <= 16 ? bwd_kt<1>(a, slices, groups, dw, st) : bwd_kt<2>(a, slices, groups, dw, st);
+  return K <= 16 ? bwd_kt<1>(a, z, slices, groups, dw, st) : bwd_kt<2>(a, z, slices, groups, dw, st);
 }
 
 // ------------------------------------------------------------------ no-allocation variant
