@@ -60,7 +60,9 @@ struct Layout {
   static constexpr int stage_bytes = x_bytes + dy_bytes + a_bytes;
   static constexpr int tx_bytes = x_bytes + dy_bytes + AR * ARB;
   static constexpr int basis_bytes = S * KP * kRowB;
-  static constexpr int red_bytes = BWD ? 2 * 8 * 16 * KP * 4 : 0;
+  // dalpha partials of RB 16-row blocks x 8 warps, reduced across warps once per RB blocks
+  static constexpr int RB = KT == 1 ? 4 : 2;
+  static constexpr int red_bytes = BWD ? RB * 8 * 16 * KP * 4 : 0;
   // with register-resident basis fragments the basis staging area is reused for the
   // dalpha reduction buffer once the fragments are loaded
   static constexpr int head_bytes =
@@ -198,6 +200,15 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
   for (int64_t it = i0; it < i1; ++it) {
     const int cur = static_cast<int>((it - i0) & 1);
     const uint32_t parity = static_cast<uint32_t>(((it - i0) >> 1) & 1);
+    const bool landed = mbar_wait(sm.bar + 8 * cur, parity);
+    if (__syncthreads_or(!landed)) {
+      if (threadIdx.x == 0) {
+        atomicOr(&g_conv_status, kStatusWaitTimeout);
+        mbar_wait(sm.bar + 8 * cur, parity);
+      }
+      return;
+    }
+    // every thread is past tile it-1, so its stage can be refilled with tile it+1
     if (threadIdx.x == 0 && it + 1 < i1) {
       int64_t ss, se, r0, r1;
       const uint32_t nbar = sm.bar + 8 * (cur ^ 1);
@@ -205,15 +216,6 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
         issue_tile<L, false>(&xmap, nullptr, &amap, sm.stages + (cur ^ 1) * L::stage_bytes, nbar, r0, ch_base);
       else
         mbar_arrive(nbar);
-    }
-    const bool landed = mbar_wait(sm.bar + 8 * cur, parity);
-    if (__syncthreads_or(!landed)) {
-      if (threadIdx.x == 0) {
-        atomicOr(&g_conv_status, kStatusWaitTimeout);
-        mbar_wait(sm.bar + 8 * cur, parity);
-        if (it + 1 < i1) mbar_wait(sm.bar + 8 * (cur ^ 1), parity ^ static_cast<uint32_t>(cur));
-      }
-      return;
     }
     if (it == i0) {
       cp_async_wait<0>();
@@ -280,7 +282,6 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
         }
       }
     }
-    __syncthreads();  // the stage is refilled by the next iteration's issue
   }
 }
 
@@ -344,11 +345,18 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
         mbar_arrive(sm.bar);
     }
   }
-  int red_buf = 0;
-
   for (int64_t it = i0; it < i1; ++it) {
     const int cur = static_cast<int>((it - i0) & 1);
     const uint32_t parity = static_cast<uint32_t>(((it - i0) >> 1) & 1);
+    const bool landed = mbar_wait(sm.bar + 8 * cur, parity);
+    if (__syncthreads_or(!landed)) {
+      if (threadIdx.x == 0) {
+        atomicOr(&g_conv_status, kStatusWaitTimeout);
+        mbar_wait(sm.bar + 8 * cur, parity);
+      }
+      return;
+    }
+    // every thread is past tile it-1, so its stage can be refilled with tile it+1
     if (threadIdx.x == 0 && it + 1 < i1) {
       int64_t ss, se, r0, r1;
       const uint32_t nbar = sm.bar + 8 * (cur ^ 1);
@@ -356,15 +364,6 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
         issue_tile<L, true>(&xmap, &dymap, &amap, sm.stages + (cur ^ 1) * L::stage_bytes, nbar, r0, ch_base);
       else
         mbar_arrive(nbar);
-    }
-    const bool landed = mbar_wait(sm.bar + 8 * cur, parity);
-    if (__syncthreads_or(!landed)) {
-      if (threadIdx.x == 0) {
-        atomicOr(&g_conv_status, kStatusWaitTimeout);
-        mbar_wait(sm.bar + 8 * cur, parity);
-        if (it + 1 < i1) mbar_wait(sm.bar + 8 * (cur ^ 1), parity ^ static_cast<uint32_t>(cur));
-      }
-      return;
     }
     if (it == i0) {
       cp_async_wait<0>();
@@ -562,25 +561,33 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
           }
         }
       }
-      float* red = red_s + (red_buf * 8 + warp) * 16 * KP;
+      // dalpha partial of this warp's 16 channels -> red_s[b % RB][warp]; the CTA adds the
+      // 8 warps once every RB blocks (and after the tile's last block)
+      float* red = red_s + ((b % L::RB) * 8 + warp) * 16 * KP;
 #pragma unroll
       for (int kn = 0; kn < 2 * KT; ++kn)
 #pragma unroll
         for (int h = 0; h < 2; ++h)
           *reinterpret_cast<float2*>(red + (g + 8 * h) * KP + kn * 8 + 2 * q) =
               make_float2(daa[kn][2 * h], daa[kn][2 * h + 1]);
-      __syncthreads();
-      const float* rb = red_s + red_buf * 8 * 16 * KP;
-      for (int o = threadIdx.x; o < 16 * KP; o += kThreads) {
-        const int row = o / KP, k = o - row * KP;
-        float sum = 0.f;
+      if (b % L::RB == L::RB - 1 || b == nb - 1) {
+        __syncthreads();
+        const int b0 = b - b % L::RB;
+        const int n_out = (b - b0 + 1) * 16 * KP;
+        for (int o = threadIdx.x; o < n_out; o += kThreads) {
+          const int blk = o / (16 * KP), rem = o - blk * 16 * KP;
+          const int row = rem / KP, k = rem - row * KP;
+          const float* rb = red_s + blk * 8 * 16 * KP + rem;
+          float sum = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) sum += rb[w * 16 * KP + o];
-        if (k < a.K && 16 * b + row < rows) a.da_part[(slice * a.n_tokens + r0 + 16 * b + row) * a.K + k] = sum;
+          for (int w = 0; w < 8; ++w) sum += rb[w * 16 * KP];
+          const int trow = 16 * (b0 + blk) + row;
+          if (k < a.K && trow < rows) a.da_part[(slice * a.n_tokens + r0 + trow) * a.K + k] = sum;
+        }
+        if (b < nb - 1) __syncthreads();  // red_s is rewritten by the next blocks of this tile
       }
-      red_buf ^= 1;
     }
-    __syncthreads();  // the stage is refilled by the next iteration's issue
+    // the next iteration's wait barrier orders these reads of red_s and the stage before reuse
   }
 
   // dbasis partial of this CTA: db_part[group][k][s][ch]
