@@ -31,6 +31,14 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
                : "r"(addr));
 }
 
+// Stores four 8x8 b16 matrices (register i = matrix i, thread t holding row t/4, columns
+// 2(t%4)..+1); lanes 8i..8i+7 give the row addresses of matrix i.
+__device__ __forceinline__ void stsm_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(r0), "r"(r1),
+               "r"(r2), "r"(r3)
+               : "memory");
+}
+
 // d += a * b  (m16n8k16, bf16 x bf16 -> fp32)
 __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(

@@ -68,7 +68,9 @@ struct Layout {
   static constexpr int head_bytes =
       align1k((BWD && BREG) ? (basis_bytes > red_bytes ? basis_bytes : red_bytes) : basis_bytes + red_bytes);
   static constexpr int dz_bytes = (BWD && ACT) ? FR * kDzRowB : 0;
-  static constexpr int total = 1024 + 2 * stage_bytes + head_bytes + dz_bytes + 64;
+  // per-warp output staging: one 16-row x 16-channel bf16 block (32-byte rows)
+  static constexpr int ost_bytes = BWD ? 0 : 8 * 16 * 32;
+  static constexpr int total = 1024 + 2 * stage_bytes + head_bytes + dz_bytes + ost_bytes + 64;
   static constexpr int min_blocks = BWD ? ((BREG && !ACT && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 3 : 2);
 };
 
@@ -97,6 +99,7 @@ struct Smem {
   char* stages_p;
   char* head;       // basis staging / dalpha reduction
   char* dz;         // fp32 dz (SiLU backward)
+  char* ost;        // per-warp output staging
   uint32_t bar;     // 2 mbarriers
   __device__ explicit Smem(char* raw) {
     char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -104,7 +107,8 @@ struct Smem {
     stages = smem_addr(base);
     head = base + 2 * L::stage_bytes;
     dz = head + L::head_bytes;
-    bar = smem_addr(dz + L::dz_bytes);
+    ost = dz + L::dz_bytes;
+    bar = smem_addr(ost + L::ost_bytes);
   }
 };
 
@@ -194,7 +198,8 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
   const int x_chunk = 2 * (warp & 3) + (lane >> 4);
   const int lrow = lm_row(lane);
   const uint32_t a_lane = static_cast<uint32_t>(lrow * L::ARB + lm_col(lane) * 2);
-  const int64_t ch_out = ch_base + warp * 16 + 2 * q;
+  const int64_t ch_stage = ch_base + warp * 16;  // the warp's first channel
+  const uint32_t ost_w = smem_addr(sm.ost + warp * 512);
 
   uint32_t bw[S][KT][4];  // basis fragments for W = alpha . basis_s (B operand, 2 channel n-tiles)
   for (int64_t it = i0; it < i1; ++it) {
@@ -239,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
       const uint32_t a_s = x_s + L::x_bytes;
       const int rows = static_cast<int>(r1 - r0);
       const int nb = (rows + 15) >> 4;
-      bf16* out_row = a.out + (r0 + g) * a.D + ch_out;
+      bf16* out_tile = a.out + r0 * a.D + ch_stage;
 #pragma unroll 1
       for (int b = 0; b < nb; ++b) {
         uint32_t af[KT][4];
@@ -266,19 +271,27 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
             ffma2(acc[nt][2], acc[nt][3], w[nt][2], w[nt][3], bf_lo(xr[2 * nt + 1]), bf_hi(xr[2 * nt + 1]));
           }
         }
+        // the block's 16 x 16 outputs go through the warp's staging rows (stmatrix) and
+        // leave as one full 32-byte row segment per lane pair
+        uint32_t o[4];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const bool row_ok = 16 * b + g + 8 * h < rows;
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            float v0 = acc[nt][2 * h], v1 = acc[nt][2 * h + 1];
-            if (ACT) {
-              v0 = silu_bf(v0);
-              v1 = silu_bf(v1);
-            }
-            if (row_ok && ch_out + nt * 8 < a.D)
-              *reinterpret_cast<uint32_t*>(out_row + (16 * b + 8 * h) * a.D + nt * 8) = pack_bf16(v0, v1);
+        for (int i = 0; i < 4; ++i) {
+          const int nt = i >> 1, h = i & 1;
+          float v0 = acc[nt][2 * h], v1 = acc[nt][2 * h + 1];
+          if (ACT) {
+            v0 = silu_bf(v0);
+            v1 = silu_bf(v1);
           }
+          o[i] = pack_bf16(v0, v1);
+        }
+        __syncwarp();  // the previous block's staging rows have been read
+        stsm_x4(ost_w + lrow * 32 + ((((lane >> 4) ^ (lrow >> 2)) & 1) << 4), o[0], o[1], o[2], o[3]);
+        __syncwarp();
+        {
+          const int row = lane >> 1, half = lane & 1;
+          const uint4 v = *reinterpret_cast<const uint4*>(sm.ost + warp * 512 + row * 32 + ((half ^ (row >> 2)) & 1) * 16);
+          if (16 * b + row < rows && ch_stage + half * 8 < a.D)
+            *reinterpret_cast<uint4*>(out_tile + (16 * b + row) * a.D + half * 8) = v;
         }
       }
     }
