@@ -214,7 +214,7 @@ typedef struct moc_decode_module {
  * agree with moc_router_forward followed by moc_step for each module within the bf16
  * tolerance: here the alpha.basis products enter an fp32 tensor-core sum exactly, where
  * moc_step (like the reference's decode kernel) rounds each product to bf16.  All modules share
- * one kernel_size; z_dim must be a multiple of 8 and every pointer 16-byte aligned.  Replaces, per module, the router
+ * one kernel_size; dim and z_dim must be multiples of 8 and every pointer 16-byte aligned.  Replaces, per module, the router
  * lines of MoC.forward (moc/api.py:383-388) and launch_update (moc/ops.py:341-362) with
  * two launches for all modules (the fused multi-module decode of the reference's
  * q / k / v usage, README.md:120-129). */

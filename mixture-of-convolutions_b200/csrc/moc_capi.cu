@@ -186,12 +186,12 @@ int moc_decode_step_multi(int32_t n_modules, const moc_decode_module* modules, i
     if (m.dim <= 0 || m.n_bases <= 0 || m.kernel_size <= 0) return MOC_ERR_INVALID_ARGUMENT;
     if ((m.activation != 0 && m.activation != 1) || (m.router_act != 0 && m.router_act != 1))
       return MOC_ERR_INVALID_ARGUMENT;
-    if (m.n_bases > 16 || m.kernel_size > 4 || m.kernel_size != S || m.dim > (int64_t{1} << 40))
+    if (m.n_bases > 16 || m.kernel_size > 4 || m.kernel_size != S || m.dim % 8 != 0 || m.dim > (int64_t{1} << 40))
       return MOC_ERR_UNSUPPORTED_SHAPE;
     if (!m.weight || !m.basis || !m.x || !m.cache || !m.alpha || !m.out) return MOC_ERR_INVALID_ARGUMENT;
     if (!a16(m.weight) || !a16(m.basis) || !a16(m.x) || !a16(m.cache) || !a16(m.alpha) || !a16(m.out))
       return MOC_ERR_MISALIGNED;
-    blocks += (m.dim + 31) / 32;
+    blocks += (m.dim + 127) / 128;
   }
   if (blocks > (int64_t{1} << 30)) return MOC_ERR_UNSUPPORTED_SHAPE;
   if (batch == 0) return MOC_OK;

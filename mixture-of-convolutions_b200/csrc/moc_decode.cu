@@ -7,17 +7,19 @@
 //                 streams z and the module's router weight for the 512-column chunks
 //                 r, r+8, ... through a 2-stage cp.async ring; its 8 warps own 64 columns
 //                 of a chunk each and accumulate the 16 x 16 logit tile with mma.sync
-//                 (bf16 -> fp32).  The partial tiles are added in shared memory, then CTA 0
-//                 adds the 8 CTAs' tiles through distributed shared memory in rank order
-//                 and applies softmax / exp per token over 16 lanes (moc/api.py:383-388).
-//   k_dec_update  CTA = (32 channels of one module, 16 tokens), warp = 8 channels.  One
-//                 mma.sync per tap forms W_s = alpha . basis_s for the warp's 16 tokens x 8
-//                 channels (bf16 products exact, fp32 sums: the rounding of the reference's
-//                 bf16 forward, moc/kernels.py:125-130; its decode kernel rounds each product
-//                 to bf16 first, moc/kernels.py:466-513, a difference far inside the bf16
-//                 tolerance).  Then y = [silu](sum_s state_s * W_s) and each channel's
-//                 cache row (S contiguous slots) is shifted and x appended
-//                 (moc/kernels.py:522-550).  All loads of a warp are issued before the math.
+//                 (bf16 -> fp32).  The partial tiles are added in shared memory, every CTA
+//                 stores its tile into CTA 0's shared memory (distributed shared memory),
+//                 and CTA 0 adds the 8 tiles in rank order and applies softmax / exp per
+//                 token over 16 lanes (moc/api.py:383-388).
+//   k_dec_update  CTA = (128 channels of one module, 16 tokens).  The basis slice, alpha,
+//                 x and cache tiles arrive with 16-byte copies; per tap, one ldmatrix of
+//                 the basis and two mma.sync per warp form W_s = alpha . basis_s for 16
+//                 tokens x 16 channels (bf16 products exact, fp32 sums: the rounding of the
+//                 reference's bf16 forward, moc/kernels.py:125-130; its decode kernel rounds
+//                 each product to bf16 first, moc/kernels.py:466-513, a difference far inside
+//                 the bf16 tolerance).  Then y = [silu](sum_s state_s * W_s), the cache rows
+//                 are shifted in shared memory with x appended (moc/kernels.py:522-550),
+//                 and y and the cache tile leave with 16-byte stores.
 #include <algorithm>
 
 #include "moc_common.cuh"
@@ -34,11 +36,24 @@ constexpr int kDecPitch = kDecCols * 2 + 16; // smem row pitch in bytes (16 B pa
 constexpr int kDecKP = 16;                   // bases per module, padded (MMA N = 2 x 8)
 constexpr int kDecStageRows = kDecTok + kDecKP;
 constexpr int kDecStageBytes = kDecStageRows * kDecPitch;
-constexpr int kDecRouterSmem = 2 * kDecStageBytes + 9 * kDecTok * kDecKP * 4;
 constexpr int kDecCluster = 8;               // CTAs per router cluster (split of z_dim)
+constexpr int kDecRouterSmem = 2 * kDecStageBytes + (8 + kDecCluster) * kDecTok * kDecKP * 4;
 constexpr int kUpdTok = 16;                  // tokens per update CTA (MMA M)
-constexpr int kUpdThreads = 128;             // 4 warps x 8 channels (MMA N)
-constexpr int kUpdCh = 32;                   // channels per update CTA
+constexpr int kUpdThreads = 256;             // 8 warps x 16 channels (two MMA n-tiles)
+constexpr int kUpdCh = 128;                  // channels per update CTA
+constexpr int kUpdBasisPitch = kUpdCh * 2 + 16;  // padded rows: conflict-free ldmatrix
+constexpr int kUpdAlphaPitch = 48;
+constexpr int kUpdWPitch = kUpdCh * 4 + 16;     // fp32 W rows, padded
+
+template <int S>
+struct UpdLayout {
+  static constexpr int basis = S * kDecKP * kUpdBasisPitch;
+  static constexpr int alpha = kUpdTok * kUpdAlphaPitch;
+  static constexpr int x = kUpdTok * kUpdCh * 2;
+  static constexpr int cache = kUpdTok * kUpdCh * S * 2;
+  static constexpr int w = S * kUpdTok * kUpdWPitch;
+  static constexpr int total = basis + alpha + x + cache + w;
+};
 
 struct DecModule {
   const bf16* w;
@@ -73,20 +88,18 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   return r;
 }
 
-// fp32 at shared address `addr` of this CTA, read from CTA `rank` of the cluster
-__device__ __forceinline__ float ld_dsmem(uint32_t addr, uint32_t rank) {
+// Stores v at shared address `addr` (this CTA's layout) of CTA `rank` of the cluster.
+__device__ __forceinline__ void st_dsmem(uint32_t addr, uint32_t rank, float v) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(addr), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(remote) : "memory");
-  return v;
+  asm volatile("st.shared::cluster.f32 [%0], %1;\n" ::"r"(remote), "f"(v) : "memory");
 }
 
 __global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(256)
     k_dec_router(const __grid_constant__ DecArgs a) {
   extern __shared__ __align__(128) char smem[];
   float* red = reinterpret_cast<float*>(smem + 2 * kDecStageBytes);  // [8 warps][16 tokens][16 bases]
-  float* part = red + 8 * kDecTok * kDecKP;                            // [16 tokens][16 bases]: this CTA's sum
+  float* part = red + 8 * kDecTok * kDecKP;  // [8 ranks][16 tokens][16 bases]: the cluster's CTA sums (rank 0's)
   const DecModule& mod = a.m[blockIdx.y];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -158,13 +171,13 @@ __global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(256)
   float l = 0.f;
 #pragma unroll
   for (int w = 0; w < 8; ++w) l += red[w * kDecTok * kDecKP + t * kDecKP + k];
-  part[t * kDecKP + k] = l;
-  cluster_sync_all();  // every CTA's partial tile is visible to the cluster
+  // every CTA puts its tile into rank 0's shared memory; rank 0 adds them in rank order
+  st_dsmem(smem_addr(part + (rank * kDecTok + t) * kDecKP + k), 0, l);
+  cluster_sync_all();
   if (rank == 0) {
-    const uint32_t addr = smem_addr(part + t * kDecKP + k);
     l = 0.f;
 #pragma unroll
-    for (uint32_t rr = 0; rr < kDecCluster; ++rr) l += ld_dsmem(addr, rr);
+    for (int rr = 0; rr < kDecCluster; ++rr) l += part[(rr * kDecTok + t) * kDecKP + k];
     float v;
     if (mod.ract == 0) {
       float mx = k < mod.K ? l : -INFINITY;
@@ -181,130 +194,155 @@ __global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(256)
     const int64_t tok = tok0 + t;
     if (tok < a.B && k < mod.K) mod.alpha[tok * mod.K + k] = __float2bfloat16_rn(v);
   }
-  cluster_sync_all();  // CTA 0 has read every partial tile before any CTA exits
-}
-
-// One channel's cache row: S contiguous bf16 slots (2*S bytes: 4-byte aligned for even S).
-template <int S>
-struct CacheRow {
-  static constexpr int kWords = (S + 1) / 2;
-  uint32_t w[kWords];  // slot i in bits 16*(i&1) of word i/2
-  __device__ __forceinline__ uint32_t slot(int i) const { return (w[i >> 1] >> (16 * (i & 1))) & 0xffffu; }
-};
-template <int S>
-__device__ __forceinline__ CacheRow<S> load_row(const bf16* p) {
-  CacheRow<S> r;
-  if constexpr (S == 4) {
-    const uint2 u = *reinterpret_cast<const uint2*>(p);
-    r.w[0] = u.x, r.w[1] = u.y;
-  } else if constexpr (S == 2) {
-    r.w[0] = *reinterpret_cast<const uint32_t*>(p);
-  } else {
-    const uint16_t* h = reinterpret_cast<const uint16_t*>(p);
-#pragma unroll
-    for (int i = 0; i < CacheRow<S>::kWords; ++i)
-      r.w[i] = h[2 * i] | (2 * i + 1 < S ? (uint32_t(h[2 * i + 1]) << 16) : 0u);
-  }
-  return r;
-}
-// Writes slots 1..S-1 of `old` to slots 0..S-2 and x to slot S-1.
-template <int S>
-__device__ __forceinline__ void store_shifted(bf16* p, const CacheRow<S>& old, uint32_t x) {
-  uint32_t v[S];
-#pragma unroll
-  for (int i = 0; i + 1 < S; ++i) v[i] = old.slot(i + 1);
-  v[S - 1] = x;
-  if constexpr (S == 4) {
-    *reinterpret_cast<uint2*>(p) = make_uint2(v[0] | (v[1] << 16), v[2] | (v[3] << 16));
-  } else if constexpr (S == 2) {
-    *reinterpret_cast<uint32_t*>(p) = v[0] | (v[1] << 16);
-  } else {
-#pragma unroll
-    for (int i = 0; i < S; ++i) reinterpret_cast<uint16_t*>(p)[i] = static_cast<uint16_t>(v[i]);
-  }
 }
 
 template <int S>
 __global__ void __launch_bounds__(kUpdThreads) k_dec_update(const __grid_constant__ DecArgs a) {
+  // tiles of this CTA's 16 tokens x 128 channels, loaded with 16-byte copies (dynamic
+  // shared memory, UpdLayout<S>)
+  extern __shared__ __align__(16) char upd_smem[];
+  using UL = UpdLayout<S>;
+  char* basis_s = upd_smem;                // [tap][base][128 ch], bases past K zero
+  char* alpha_s = basis_s + UL::basis;     // [token][16 bases]
+  char* x_s = alpha_s + UL::alpha;         // [token][128 ch]; y replaces x in place
+  char* cache_s = x_s + UL::x;             // [token][128 ch][S]
+  char* w_s = cache_s + UL::cache;         // [tap][token][128 ch] fp32
+  char* y_s = x_s;
   int m = 0;
   while (m + 1 < a.n_mod && static_cast<int>(blockIdx.x) >= a.blk_prefix[m + 1]) ++m;
   const DecModule& mod = a.m[m];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
-  const int64_t cw = static_cast<int64_t>(static_cast<int>(blockIdx.x) - a.blk_prefix[m]) * kUpdCh + warp * 8;
+  const int64_t c0 = static_cast<int64_t>(static_cast<int>(blockIdx.x) - a.blk_prefix[m]) * kUpdCh;
   const int64_t b0 = static_cast<int64_t>(blockIdx.y) * kUpdTok;
-  if (cw >= mod.D) return;  // whole warp
-  const uint16_t* al = reinterpret_cast<const uint16_t*>(mod.alpha);
-  const uint16_t* bs = reinterpret_cast<const uint16_t*>(mod.basis);
-  const uint16_t* xs = reinterpret_cast<const uint16_t*>(mod.x);
+  const int nch = static_cast<int>(mod.D - c0 < kUpdCh ? mod.D - c0 : kUpdCh);  // multiple of 8
+  const int ntok = static_cast<int>(a.B - b0 < kUpdTok ? a.B - b0 : kUpdTok);
 
-  // every load of the warp's tile first (one round trip): B operand = basis of channel
-  // cw + g (n) and bases 2q.. / 2q+8.. (k) per tap; A operand = alpha of tokens b0 + g,
-  // b0 + g + 8 and the same bases; x and cache rows of (tokens b0+g, b0+g+8) x
-  // (channels cw+2q, cw+2q+1).  Bases past K, channels past D and tokens past B read 0.
-  auto ld = [](const uint16_t* p, int64_t i, bool ok) -> uint32_t { return ok ? p[i] : 0u; };
-  uint32_t bf[S][2];
-  {
-    const int64_t ch = cw + g;
-#pragma unroll
-    for (int s = 0; s < S; ++s)
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int k = 2 * q + 8 * j;
-        bf[s][j] = ld(bs, (static_cast<int64_t>(k) * S + s) * mod.D + ch, ch < mod.D && k < mod.K) |
-                   (ld(bs, (static_cast<int64_t>(k + 1) * S + s) * mod.D + ch, ch < mod.D && k + 1 < mod.K) << 16);
-      }
+  // ---- loads (16-byte pieces; missing channels, tokens and bases become zeros)
+  constexpr int kPieces = kUpdCh / 8;  // 16-byte pieces per 64-channel row
+  for (int i = threadIdx.x; i < S * kDecKP * kPieces; i += kUpdThreads) {
+    const int row = i / kPieces, p = i - row * kPieces;  // row = s * 16 + k
+    const int s = row / kDecKP, k = row - s * kDecKP;
+    const bool ok = k < mod.K && p * 8 < nch;
+    cp_async16(smem_addr(basis_s + row * kUpdBasisPitch + p * 16),
+               ok ? mod.basis + (static_cast<int64_t>(k) * S + s) * mod.D + c0 + p * 8 : mod.basis, ok ? 16u : 0u);
   }
+  for (int i = threadIdx.x; i < kUpdTok * kPieces; i += kUpdThreads) {
+    const int t = i / kPieces, p = i - t * kPieces;
+    const bool ok = t < ntok && p * 8 < nch;
+    cp_async16(smem_addr(x_s + t * kUpdCh * 2 + p * 16), ok ? mod.x + (b0 + t) * mod.D + c0 + p * 8 : mod.x,
+               ok ? 16u : 0u);
+  }
+  for (int i = threadIdx.x; i < kUpdTok * kPieces * S; i += kUpdThreads) {
+    const int t = i / (kPieces * S), p = i - t * kPieces * S;  // 16-byte piece p of the token's row
+    const bool ok = t < ntok && p * 8 < nch * S;
+    cp_async16(smem_addr(cache_s + t * kUpdCh * S * 2 + p * 16),
+               ok ? mod.cache + ((b0 + t) * mod.D + c0) * S + p * 8 : mod.cache, ok ? 16u : 0u);
+  }
+  cp_async_commit();
+  for (int i = threadIdx.x; i < kUpdTok * kDecKP; i += kUpdThreads) {
+    const int t = i / kDecKP, k = i - t * kDecKP;
+    const bool ok = t < ntok && k < mod.K;
+    reinterpret_cast<bf16*>(alpha_s + t * kUpdAlphaPitch)[k] = ok ? mod.alpha[(b0 + t) * mod.K + k] : bf16(0.f);
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // ---- W_s = alpha . basis_s for the warp's 16 channels (two 8-channel n-tiles) and the
+  // CTA's 16 tokens, into w_s [tap][token][64 channels] fp32
   uint32_t af[4];
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int64_t b = b0 + g + 8 * (r & 1);
-    const int k = 2 * q + 8 * (r >> 1);
-    af[r] = ld(al, b * mod.K + k, b < a.B && k < mod.K) | (ld(al, b * mod.K + k + 1, b < a.B && k + 1 < mod.K) << 16);
-  }
-  uint32_t xv[2][2];
-  CacheRow<S> cr[2][2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int64_t b = b0 + g + 8 * h, ch = cw + 2 * q + e;
-      const bool ok = b < a.B && ch < mod.D;
-      xv[h][e] = ld(xs, b * mod.D + ch, ok);
-#pragma unroll
-      for (int i = 0; i < CacheRow<S>::kWords; ++i) cr[h][e].w[i] = 0;
-      if (ok) cr[h][e] = load_row<S>(mod.cache + (b * mod.D + ch) * S);
-    }
-
-  // W_s = alpha . basis_s for 16 tokens x 8 channels per tap (fp32 accumulate), then
-  // y = sum_s state_s * W_s with state_s = cache slot s+1, x for the newest tap
-  float acc[2][2] = {};
+  ldsm_x4(smem_addr(alpha_s) + lm_row_d(lane) * kUpdAlphaPitch + lm_col_d(lane) * 2, af);
+  const int cw = warp * 16;
 #pragma unroll
   for (int s = 0; s < S; ++s) {
-    float w[4];
-    mma_bf16_z(w, af, bf[s][0], bf[s][1]);  // w[2h + e]: token b0+g+8h, channel cw+2q+e
+    uint32_t bf[4];
+    ldsm_x4_t(smem_addr(basis_s) + (s * kDecKP + lm_row_d(lane)) * kUpdBasisPitch + (cw + lm_col_d(lane)) * 2, bf);
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+    for (int nt = 0; nt < 2; ++nt) {
+      float w[4];
+      mma_bf16_z(w, af, bf[2 * nt], bf[2 * nt + 1]);  // w[2h + e]: token g + 8h, channel cw + 8nt + 2q + e
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const uint32_t st = s == S - 1 ? xv[h][e] : cr[h][e].slot(s + 1);
-        acc[h][e] = fmaf(__uint_as_float(st << 16), w[2 * h + e], acc[h][e]);
-      }
-  }
-#pragma unroll
-  for (int h = 0; h < 2; ++h)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int64_t b = b0 + g + 8 * h, ch = cw + 2 * q + e;
-      if (b < a.B && ch < mod.D) {
-        const float v = mod.act ? silu_f(acc[h][e]) : acc[h][e];
-        mod.out[b * mod.D + ch] = __float2bfloat16_rn(v);
-        store_shifted<S>(mod.cache + (b * mod.D + ch) * S, cr[h][e], xv[h][e]);
-      }
+      for (int h = 0; h < 2; ++h)
+        *reinterpret_cast<float2*>(w_s + (s * kUpdTok + g + 8 * h) * kUpdWPitch + (cw + 8 * nt + 2 * q) * 4) =
+            make_float2(w[2 * h], w[2 * h + 1]);
     }
+  }
+  __syncthreads();
+
+  // ---- thread = (token, channel pair): y = [silu](sum_s state_s * W_s) with state_s = cache
+  // slot s+1, x for the newest tap; the pair's two cache rows shift in place, x appended
+#pragma unroll
+  for (int it = 0; it < kUpdTok * (kUpdCh / 2) / kUpdThreads; ++it) {
+    const int item = it * kUpdThreads + threadIdx.x;
+    const int t = item / (kUpdCh / 2), ch = 2 * (item - t * (kUpdCh / 2));
+    const uint32_t xp = *reinterpret_cast<const uint32_t*>(x_s + (t * kUpdCh + ch) * 2);
+    uint32_t cr[S];  // rows of channels ch, ch+1: S slots each, 2*S bf16
+    char* crow = cache_s + (t * kUpdCh + ch) * S * 2;
+#pragma unroll
+    for (int i = 0; i < S; ++i) cr[i] = reinterpret_cast<const uint32_t*>(crow)[i];
+    auto slot = [&](int e, int i) -> uint32_t {  // channel ch+e, slot i
+      const int el = e * S + i;
+      return (cr[el >> 1] >> (16 * (el & 1))) & 0xffffu;
+    };
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      const float2 w = *reinterpret_cast<const float2*>(w_s + (s * kUpdTok + t) * kUpdWPitch + ch * 4);
+      const uint32_t s0 = s == S - 1 ? (xp & 0xffffu) : slot(0, s + 1);
+      const uint32_t s1 = s == S - 1 ? (xp >> 16) : slot(1, s + 1);
+      acc0 = fmaf(__uint_as_float(s0 << 16), w.x, acc0);
+      acc1 = fmaf(__uint_as_float(s1 << 16), w.y, acc1);
+    }
+    if (mod.act) {
+      acc0 = silu_f(acc0);
+      acc1 = silu_f(acc1);
+    }
+    *reinterpret_cast<uint32_t*>(y_s + (t * kUpdCh + ch) * 2) = pack_bf16(acc0, acc1);
+    uint32_t nr[S];
+#pragma unroll
+    for (int i = 0; i < S; ++i) {
+      uint32_t half[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int el = 2 * i + j, e = el / S, sl = el - e * S;
+        half[j] = sl == S - 1 ? (e == 0 ? (xp & 0xffffu) : (xp >> 16)) : slot(e, sl + 1);
+      }
+      nr[i] = half[0] | (half[1] << 16);
+    }
+#pragma unroll
+    for (int i = 0; i < S; ++i) reinterpret_cast<uint32_t*>(crow)[i] = nr[i];
+  }
+  __syncthreads();
+
+  // ---- stores (16-byte pieces)
+  for (int i = threadIdx.x; i < kUpdTok * kPieces; i += kUpdThreads) {
+    const int t = i / kPieces, p = i - t * kPieces;
+    if (t < ntok && p * 8 < nch)
+      *reinterpret_cast<uint4*>(mod.out + (b0 + t) * mod.D + c0 + p * 8) =
+          *reinterpret_cast<const uint4*>(y_s + t * kUpdCh * 2 + p * 16);
+  }
+  for (int i = threadIdx.x; i < kUpdTok * kPieces * S; i += kUpdThreads) {
+    const int t = i / (kPieces * S), p = i - t * kPieces * S;
+    if (t < ntok && p * 8 < nch * S)
+      *reinterpret_cast<uint4*>(mod.cache + ((b0 + t) * mod.D + c0) * S + p * 8) =
+          *reinterpret_cast<const uint4*>(cache_s + t * kUpdCh * S * 2 + p * 16);
+  }
 }
 
 int g_dec_sm_configured[64];
+
+template <int S>
+cudaError_t launch_update(dim3 grid, const DecArgs& a, cudaStream_t st, int dev) {
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k_dec_update<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, UpdLayout<S>::total);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  k_dec_update<S><<<grid, kUpdThreads, UpdLayout<S>::total, st>>>(a);
+  return cudaSuccess;
+}
 
 }  // namespace
 
@@ -346,12 +384,13 @@ int decode_step_multi(int n, const moc_decode_module* mods, int64_t B, int64_t D
   if (e != cudaSuccess) return note_cuda(e);
   const dim3 grid(static_cast<unsigned>(a.blk_prefix[n]), static_cast<unsigned>(ceil_div(B, kUpdTok)));
   switch (S) {
-    case 1: k_dec_update<1><<<grid, kUpdThreads, 0, st>>>(a); break;
-    case 2: k_dec_update<2><<<grid, kUpdThreads, 0, st>>>(a); break;
-    case 3: k_dec_update<3><<<grid, kUpdThreads, 0, st>>>(a); break;
-    case 4: k_dec_update<4><<<grid, kUpdThreads, 0, st>>>(a); break;
+    case 1: e = launch_update<1>(grid, a, st, dev); break;
+    case 2: e = launch_update<2>(grid, a, st, dev); break;
+    case 3: e = launch_update<3>(grid, a, st, dev); break;
+    case 4: e = launch_update<4>(grid, a, st, dev); break;
     default: return MOC_ERR_UNSUPPORTED_SHAPE;
   }
+  if (e != cudaSuccess) return note_cuda(e);
   note_launch();
   return note_cuda(cudaGetLastError());
 }

@@ -9,7 +9,8 @@ over z, the other mixes, convolves and shifts every module's cache.
 
 Results match calling ``module.step(x, z, cache)`` for each module; shapes the fused
 kernels do not cover (fp32 or fp16 modules, more than 16 bases, kernel sizes above 4,
-mixed kernel sizes, more than four modules) take that per-module path.
+mixed kernel sizes, dims that are not a multiple of 8, more than four modules) take that
+per-module path.
 """
 from __future__ import annotations
 
@@ -48,7 +49,7 @@ def _fusable(modules: Sequence[MoC], xs, z, caches) -> bool:
             return False
         if x.dtype != torch.bfloat16 or c.dtype != torch.bfloat16 or not c.is_contiguous():
             return False
-        if m.k > 16 or m.kernel_size != S or S > 4:
+        if m.k > 16 or m.kernel_size != S or S > 4 or m.dim % 8 != 0:
             return False
         if c.data_ptr() % 16 != 0:
             return False

@@ -152,6 +152,7 @@ def test_decode_multi_checks():
     assert lib.moc_decode_step_multi(1, mods(1, n_bases=17), 4, 64, 2048, None) == 3
     assert lib.moc_decode_step_multi(1, mods(1, kernel_size=5), 4, 64, 2048, None) == 3
     assert lib.moc_decode_step_multi(1, mods(1, dim=0), 4, 64, 2048, None) == 1
+    assert lib.moc_decode_step_multi(1, mods(1, dim=60), 4, 64, 2048, None) == 3  # dim % 8
     assert lib.moc_decode_step_multi(1, mods(1), 4, 60, 2048, None) == 3  # z_dim % 8
     assert lib.moc_decode_step_multi(1, mods(1, router_act=2), 4, 64, 2048, None) == 1
     assert lib.moc_decode_step_multi(1, mods(1, cache=1030), 4, 64, 2048, None) == 4

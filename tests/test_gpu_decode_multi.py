@@ -73,8 +73,12 @@ def test_qkv_shaped_modules():
 
 @pytest.mark.parametrize("ks", [1, 2, 3, 4])
 def test_kernel_sizes_bases_and_silu(ks):
-    _run([(96, 8, "softmax", "silu"), (258, 16, "exp", None), (37, 5, "exp", "silu")], B=5, z_dim=520, ks=ks,
+    _run([(96, 8, "softmax", "silu"), (264, 16, "exp", None), (40, 5, "exp", "silu")], B=5, z_dim=520, ks=ks,
          seed=ks)
+
+
+def test_dims_off_the_8_channel_grid_take_the_per_module_path():
+    _run([(258, 16, "exp", None), (37, 5, "softmax", "silu")], B=5, z_dim=64, ks=4, steps=2)
 
 
 def test_single_module_and_single_sequence():
