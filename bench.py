@@ -442,7 +442,13 @@ def main() -> None:
     x = host["x"].to(device).requires_grad_()
     z = host["z"].to(device).requires_grad_()
     dy = host["dy"].to(device)
-    reducer = dp.GradAllReduce([m.conv_bases, m.router]) if world > 1 else None
+    # the step's one collective: this library's NVLink all-reduce (MOC_ALLREDUCE=nccl: NCCL)
+    reducer = None
+    if world > 1:
+        if os.environ.get("MOC_ALLREDUCE", "nvlink") == "nccl":
+            reducer = dp.GradAllReduce([m.conv_bases, m.router])
+        else:
+            reducer = dp.NVLinkGradAllReduce([m.conv_bases, m.router])
 
     # --- device-resident step, captured in a CUDA graph
     side = torch.cuda.Stream(device)
@@ -529,9 +535,9 @@ def main() -> None:
         kernel_ms[name] = graph_time(fn, reps, device)
     allreduce_ms = None
     if reducer is not None:  # every rank: the same collectives in the same order
-        flat = torch.zeros_like(reducer.flat)
+        gcopy = [g.clone() for g in g_grads[2:]]
         barrier(world)
-        allreduce_ms = max_over_ranks(time_region(lambda: dist.all_reduce(flat), 10, stream), world)
+        allreduce_ms = max_over_ranks(time_region(lambda: reducer(gcopy), 10, stream), world)
     dominant = max(kernel_ms, key=kernel_ms.get)
     peaks = measured_peaks()
     kbytes = KERNEL_BYTES_PER_TOKEN[dominant](cfg) * N_rank
@@ -577,6 +583,9 @@ def main() -> None:
     sampler.stop()
     del graph
     if world > 1:
+        dist.barrier()
+        if hasattr(reducer, "close"):
+            reducer.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -221,6 +221,34 @@ typedef struct moc_decode_module {
 int moc_decode_step_multi(int32_t n_modules, const moc_decode_module* modules, int64_t batch,
                           int64_t z_dim, const void* z, void* stream);
 
+/* Gradient all-reduce over NVLink peer memory, for the data-parallel step (one process
+ * per GPU).  The step's only collective sums the parameter gradients (conv_bases and
+ * router) over ranks; at 640 KiB it is latency-bound, and this replaces the NCCL
+ * all-reduce by one kernel that reads every rank's slice through CUDA IPC peer pointers.
+ *
+ * Setup, once per rank with its device current: moc_comm_create allocates this rank's
+ * exchange buffer (2 x capacity fp32 plus flags; the only allocating calls of the
+ * library are create / destroy) and writes its IPC handle (MOC_IPC_HANDLE_BYTES) to
+ * handle_out; the caller gathers the world's handles in rank order (e.g. with
+ * torch.distributed.all_gather_object) and passes them to moc_comm_connect.
+ *
+ * moc_comm_allreduce sums, in place on every rank, up to MOC_COMM_MAX_SEGMENTS device
+ * arrays (data[i], counts[i] elements of dtypes[i]: fp32, fp16 or bf16), accumulating in
+ * fp32 in rank order so every rank gets bitwise the same result.  Every rank must make
+ * the same calls in the same order.  The call is stream-ordered and can be captured in a
+ * CUDA graph.  A rank that waits too long for its peers records MOC_STATUS_WAIT_TIMEOUT
+ * (see moc_device_status) and leaves its data unchanged.  No counterpart in the
+ * reference, which trains in one process. */
+#define MOC_COMM_MAX_RANKS 8
+#define MOC_COMM_MAX_SEGMENTS 4
+#define MOC_IPC_HANDLE_BYTES 64
+typedef struct moc_comm moc_comm;
+int moc_comm_create(int32_t rank, int32_t world, int64_t capacity, moc_comm** comm, void* handle_out);
+int moc_comm_connect(moc_comm* comm, const void* handles);
+int moc_comm_allreduce(moc_comm* comm, int32_t n_segments, void* const* data, const int64_t* counts,
+                       const int32_t* dtypes, void* stream);
+int moc_comm_destroy(moc_comm* comm);
+
 #ifdef __cplusplus
 }
 #endif

@@ -108,11 +108,12 @@ uint64_t moc_launch_count(void) { return g_launches.load(std::memory_order_relax
 
 int moc_device_status(int* status, int clear) {
   if (status == nullptr) return MOC_ERR_INVALID_ARGUMENT;
-  int r = 0, c = 0;
+  int r = 0, c = 0, m = 0;
   int rc = router_status(&r, clear != 0);
   if (rc == MOC_OK) rc = conv_status(&c, clear != 0);
+  if (rc == MOC_OK) rc = comm_status(&m, clear != 0);
   if (rc != MOC_OK) return rc;
-  *status = r | c;
+  *status = r | c | m;
   return MOC_OK;
 }
 
@@ -198,6 +199,38 @@ int moc_decode_step_multi(int32_t n_modules, const moc_decode_module* modules, i
   if (!z) return MOC_ERR_INVALID_ARGUMENT;
   if (!a16(z)) return MOC_ERR_MISALIGNED;
   return decode_step_multi(n_modules, modules, batch, z_dim, z, static_cast<cudaStream_t>(stream));
+}
+
+int moc_comm_create(int32_t rank, int32_t world, int64_t capacity, moc_comm** comm, void* handle_out) {
+  if (!comm || !handle_out || world < 1 || world > MOC_COMM_MAX_RANKS || rank < 0 || rank >= world || capacity <= 0)
+    return MOC_ERR_INVALID_ARGUMENT;
+  if (capacity > (int64_t{1} << 34)) return MOC_ERR_UNSUPPORTED_SHAPE;
+  CommImpl* c = nullptr;
+  const int rc = comm_create(rank, world, capacity, &c, handle_out);
+  if (rc == MOC_OK) *comm = reinterpret_cast<moc_comm*>(c);
+  return rc;
+}
+
+int moc_comm_connect(moc_comm* comm, const void* handles) {
+  if (!comm || !handles) return MOC_ERR_INVALID_ARGUMENT;
+  return comm_connect(reinterpret_cast<CommImpl*>(comm), handles);
+}
+
+int moc_comm_allreduce(moc_comm* comm, int32_t n_segments, void* const* data, const int64_t* counts,
+                       const int32_t* dtypes, void* stream) {
+  if (!comm || n_segments < 0 || n_segments > MOC_COMM_MAX_SEGMENTS || (n_segments > 0 && (!data || !counts || !dtypes)))
+    return MOC_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < n_segments; ++i) {
+    if (!valid_float_dtype(dtypes[i])) return MOC_ERR_UNSUPPORTED_DTYPE;
+    if (counts[i] < 0 || (counts[i] > 0 && !data[i])) return MOC_ERR_INVALID_ARGUMENT;
+  }
+  return comm_allreduce(reinterpret_cast<CommImpl*>(comm), n_segments, data, counts, dtypes,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int moc_comm_destroy(moc_comm* comm) {
+  if (!comm) return MOC_ERR_INVALID_ARGUMENT;
+  return comm_destroy(reinterpret_cast<CommImpl*>(comm));
 }
 
 int moc_router_forward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t dtype, int32_t router_act,

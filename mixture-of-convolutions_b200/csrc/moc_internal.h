@@ -53,6 +53,16 @@ int tc_router_backward_noalloc(int64_t N, int64_t Dz, int K, int act, const void
 // fused decode step of up to MOC_DECODE_MAX_MODULES modules sharing z (moc_decode.cu)
 int decode_step_multi(int n, const moc_decode_module* mods, int64_t B, int64_t Dz, const void* z, cudaStream_t st);
 
+// gradient all-reduce over NVLink peer memory (moc_comm.cu); CommImpl is the object
+// behind the C ABI's opaque moc_comm
+struct CommImpl;
+int comm_create(int rank, int world, int64_t capacity, CommImpl** out, void* handle_out);
+int comm_connect(CommImpl* c, const void* handles);
+int comm_allreduce(CommImpl* c, int n_seg, void* const* data, const int64_t* n, const int32_t* dtype,
+                   cudaStream_t st);
+int comm_destroy(CommImpl* c);
+int comm_status(int* out, bool clear);
+
 // device status words of the TMA-staged kernels (bounded-wait timeouts), read/cleared
 // by moc_device_status(); and a probe kernel that exercises the timeout path.
 int router_status(int* out, bool clear);

@@ -100,7 +100,15 @@ SIGNATURES = {
     ),
     "moc_prepare_chunk_indices": (ctypes.c_int, [_P, _I32, _I64, _I32, _P, _I64, _P]),
     "moc_decode_step_multi": (ctypes.c_int, [_I32, ctypes.POINTER(MocDecodeModule), _I64, _I64, _P, _P]),
+    "moc_comm_create": (ctypes.c_int, [_I32, _I32, _I64, ctypes.POINTER(_P), _P]),
+    "moc_comm_connect": (ctypes.c_int, [_P, _P]),
+    "moc_comm_allreduce": (ctypes.c_int, [_P, _I32, ctypes.POINTER(_P), ctypes.POINTER(_I64), ctypes.POINTER(_I32), _P]),
+    "moc_comm_destroy": (ctypes.c_int, [_P]),
 }
+
+COMM_MAX_RANKS = 8
+COMM_MAX_SEGMENTS = 4
+IPC_HANDLE_BYTES = 64
 
 _lib = None
 _lock = threading.Lock()

@@ -12,10 +12,13 @@ scaling layer of this build, used by bench.py for the multi-GPU runs.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Iterable, Sequence
 
 import torch
 import torch.distributed as dist
+
+from . import _lib
 
 
 def shard_fixed(batch: int, rank: int, world: int) -> slice:
@@ -92,3 +95,65 @@ class GradAllReduce:
             off += n
         return grads
 
+
+
+class NVLinkGradAllReduce:
+    """The same sum as GradAllReduce, by this library's own NVLink kernel instead of NCCL
+    (``moc_comm_*`` in include/moc_b200.h): every rank's exchange buffer is opened by the
+    others through CUDA IPC, and one kernel per call publishes this rank's gradients, waits
+    (bounded) for the other ranks' and adds all of them in rank order, so every rank holds
+    bitwise the same sum.  One process per GPU, all ranks on one node (peer access over
+    NVLink / NVSwitch), at most 8 ranks, up to 4 gradient tensors.  Setup exchanges the IPC
+    handles with ``all_gather_object`` over ``group``; each call is stream-ordered and can be
+    captured in a CUDA graph.  Every rank must make the same calls in the same order."""
+
+    def __init__(self, params: Iterable[torch.Tensor], group=None):
+        self.params = list(params)
+        if not 1 <= len(self.params) <= _lib.COMM_MAX_SEGMENTS:
+            raise ValueError(f"between 1 and {_lib.COMM_MAX_SEGMENTS} parameters")
+        dev = self.params[0].device
+        if dev.type != "cuda":
+            raise ValueError("NVLinkGradAllReduce needs CUDA parameters")
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        if world > _lib.COMM_MAX_RANKS:
+            raise ValueError(f"at most {_lib.COMM_MAX_RANKS} ranks")
+        self.device = dev
+        lib = _lib.load()
+        handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+        comm = ctypes.c_void_p()
+        with torch.cuda.device(dev):
+            _lib.check(lib.moc_comm_create(rank, world, sum(p.numel() for p in self.params), ctypes.byref(comm),
+                                           handle), "moc_comm_create")
+        self._comm = comm
+        handles = [None] * world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        blob = ctypes.create_string_buffer(b"".join(handles), world * _lib.IPC_HANDLE_BYTES)
+        with torch.cuda.device(dev):
+            _lib.check(lib.moc_comm_connect(comm, blob), "moc_comm_connect")
+        dist.barrier(group=group)  # every rank is connected before any kernel waits on a peer
+
+    def __call__(self, grads: Sequence[torch.Tensor] | None = None) -> list[torch.Tensor]:
+        """All-reduce `grads` (default: each parameter's .grad) in place; returns them."""
+        grads = [p.grad for p in self.params] if grads is None else list(grads)
+        if len(grads) != len(self.params) or any(g is None for g in grads):
+            raise ValueError("one gradient per parameter is required")
+        for g, p in zip(grads, self.params):
+            if not g.is_contiguous() or g.numel() != p.numel() or g.device != self.device:
+                raise ValueError("gradients must be contiguous, parameter-shaped and on the parameters' device")
+        n = len(grads)
+        ptrs = (ctypes.c_void_p * n)(*[g.data_ptr() for g in grads])
+        counts = (ctypes.c_int64 * n)(*[g.numel() for g in grads])
+        dtypes = (ctypes.c_int32 * n)(*[_lib.dtype_code(g) for g in grads])
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.load().moc_comm_allreduce(self._comm, n, ptrs, counts, dtypes,
+                                                      _lib.stream_of(self.device)), "moc_comm_allreduce")
+        return grads
+
+    def close(self) -> None:
+        """Frees the exchange buffer (after every rank's last call has finished)."""
+        if self._comm:
+            torch.cuda.synchronize(self.device)
+            with torch.cuda.device(self.device):
+                _lib.check(_lib.load().moc_comm_destroy(self._comm), "moc_comm_destroy")
+            self._comm = None

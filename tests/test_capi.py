@@ -161,3 +161,16 @@ def test_decode_multi_checks():
     two[1].kernel_size = 2
     assert lib.moc_decode_step_multi(2, two, 4, 64, 2048, None) == 3  # one kernel size for all modules
     assert lib.moc_decode_step_multi(2, mods(2), 0, 64, 2048, None) == 0  # empty batch: no work
+
+
+def test_comm_checks():
+    lib = _lib.load()
+    comm = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    assert lib.moc_comm_create(0, 0, 16, ctypes.byref(comm), handle) == 1
+    assert lib.moc_comm_create(2, 2, 16, ctypes.byref(comm), handle) == 1
+    assert lib.moc_comm_create(0, 9, 16, ctypes.byref(comm), handle) == 1  # more than 8 ranks
+    assert lib.moc_comm_create(0, 1, 0, ctypes.byref(comm), handle) == 1
+    assert lib.moc_comm_connect(None, handle) == 1
+    assert lib.moc_comm_allreduce(None, 0, None, None, None, None) == 1
+    assert lib.moc_comm_destroy(None) == 1
