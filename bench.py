@@ -445,10 +445,13 @@ def main() -> None:
     # the step's one collective: this library's NVLink all-reduce (MOC_ALLREDUCE=nccl: NCCL)
     reducer = None
     if world > 1:
-        if os.environ.get("MOC_ALLREDUCE", "nvlink") == "nccl":
+        if os.environ.get("MOC_ALLREDUCE", "nvlink") != "nccl":
+            try:  # every rank raises together if any rank cannot set up peer access
+                reducer = dp.NVLinkGradAllReduce([m.conv_bases, m.router])
+            except RuntimeError as e:
+                print(f"rank {rank}: NVLink all-reduce unavailable ({e}); using NCCL", file=sys.stderr)
+        if reducer is None:
             reducer = dp.GradAllReduce([m.conv_bases, m.router])
-        else:
-            reducer = dp.NVLinkGradAllReduce([m.conv_bases, m.router])
 
     # --- device-resident step, captured in a CUDA graph
     side = torch.cuda.Stream(device)
@@ -570,6 +573,7 @@ def main() -> None:
                          "algorithmic_bytes_per_launch": kbytes},
             "kernel_ms": kernel_ms,
             "grad_allreduce_ms": allreduce_ms,
+            "grad_allreduce": type(reducer).__name__ if reducer is not None else None,
             "e2e": {"value": tokens_all / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
             "gpu_launches": launches_per_step * args.steps,

@@ -30,7 +30,7 @@ __device__ int g_comm_status;
 
 namespace {
 
-constexpr int kCommCtas = 64;
+constexpr int kCommCtas = 128;
 constexpr int kCommThreads = 256;
 constexpr uint32_t kCommPollLimit = 1u << 22;
 

@@ -119,19 +119,35 @@ class NVLinkGradAllReduce:
         if world > _lib.COMM_MAX_RANKS:
             raise ValueError(f"at most {_lib.COMM_MAX_RANKS} ranks")
         self.device = dev
+        self._comm = None
         lib = _lib.load()
+        # every step of the setup ends with an agreement over `group`, so a failure on one
+        # rank raises on all of them instead of leaving the others waiting
         handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
         comm = ctypes.c_void_p()
         with torch.cuda.device(dev):
-            _lib.check(lib.moc_comm_create(rank, world, sum(p.numel() for p in self.params), ctypes.byref(comm),
-                                           handle), "moc_comm_create")
-        self._comm = comm
+            rc = lib.moc_comm_create(rank, world, sum(p.numel() for p in self.params), ctypes.byref(comm), handle)
+        if rc == _lib.MOC_OK:
+            self._comm = comm
+        self._agree(rc == _lib.MOC_OK, "moc_comm_create", rc, group)
         handles = [None] * world
         dist.all_gather_object(handles, handle.raw, group=group)
         blob = ctypes.create_string_buffer(b"".join(handles), world * _lib.IPC_HANDLE_BYTES)
         with torch.cuda.device(dev):
-            _lib.check(lib.moc_comm_connect(comm, blob), "moc_comm_connect")
-        dist.barrier(group=group)  # every rank is connected before any kernel waits on a peer
+            rc = lib.moc_comm_connect(comm, blob)
+        self._agree(rc == _lib.MOC_OK, "moc_comm_connect", rc, group)
+
+    def _agree(self, ok: bool, what: str, rc: int, group) -> None:
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32)
+        if dist.get_backend(group) == "nccl":
+            flag = flag.to(self.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+        if int(flag.item()) == 1:
+            return
+        self.close(sync=False)
+        if not ok:
+            _lib.check(rc, what)
+        raise RuntimeError(f"{what} failed on another rank")
 
     def __call__(self, grads: Sequence[torch.Tensor] | None = None) -> list[torch.Tensor]:
         """All-reduce `grads` (default: each parameter's .grad) in place; returns them."""
@@ -150,10 +166,12 @@ class NVLinkGradAllReduce:
                                                       _lib.stream_of(self.device)), "moc_comm_allreduce")
         return grads
 
-    def close(self) -> None:
+    def close(self, sync: bool = True) -> None:
         """Frees the exchange buffer (after every rank's last call has finished)."""
         if self._comm:
-            torch.cuda.synchronize(self.device)
+            if sync:
+                torch.cuda.synchronize(self.device)
             with torch.cuda.device(self.device):
-                _lib.check(_lib.load().moc_comm_destroy(self._comm), "moc_comm_destroy")
+                rc = _lib.load().moc_comm_destroy(self._comm)
             self._comm = None
+            _lib.check(rc, "moc_comm_destroy")
