@@ -72,6 +72,13 @@ typedef struct moc_problem {
   int32_t chunk_indices_dtype;
   int64_t n_chunks;
   int32_t chunk_size;
+  /* Optional, fixed length only: the conv cache [batch, dim, kernel_size] (x's dtype,
+   * element strides halo_strides) of the tokens before each sequence.  The taps of the
+   * first kernel_size - 1 positions then read those tokens (slot S-1 newest) instead of
+   * zeros, which is prefill with a cache (the reference prepends the cache with zero
+   * routing weights, moc/api.py:299-309).  The cache itself gets no gradient. */
+  const void* halo;
+  int64_t halo_strides[3];
 } moc_problem;
 
 /* Library identification, e.g. "moc_b200 0.1.0 sm_100a". */

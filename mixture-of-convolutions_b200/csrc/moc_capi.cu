@@ -44,6 +44,10 @@ static int check_problem(const moc_problem* p) {
       return MOC_ERR_UNSUPPORTED_DTYPE;
     if (p->n_chunks > 0 && p->chunk_indices == nullptr) return MOC_ERR_INVALID_ARGUMENT;
   }
+  if (p->halo != nullptr) {  // a cache precedes fixed-length sequences only
+    if (p->cu_seqlens != nullptr) return MOC_ERR_INVALID_ARGUMENT;
+    if (p->halo_strides[0] < 0 || p->halo_strides[1] < 0 || p->halo_strides[2] < 0) return MOC_ERR_INVALID_ARGUMENT;
+  }
   return MOC_OK;
 }
 

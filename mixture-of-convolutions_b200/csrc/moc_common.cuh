@@ -103,7 +103,23 @@ struct RowMap {
   int64_t n_chunks = 0;
   int32_t chunk_size = 0;
 
+  // fixed length with a cache: the tokens before each sequence (cache [batch, D, S], slot S-1
+  // newest), read by the causal taps instead of zeros
+  const void* halo = nullptr;
+  int64_t hs0 = 0, hs1 = 0, hs2 = 0;
+  int32_t halo_S = 0, halo_dt = 0;
+
   __host__ __device__ int64_t n_items() const { return varlen ? n_chunks : batch * tiles_per_seq; }
+
+  // x value of token `src` < `seq_start` (m = seq_start - src tokens back) for channel d:
+  // the cache slot S - m when a cache is attached and m < S, else 0
+  __device__ __forceinline__ float halo_at(int64_t seq_start, int64_t src, int64_t d) const {
+    if (halo == nullptr || varlen) return 0.f;
+    const int64_t m = seq_start - src;
+    if (m < 1 || m >= halo_S) return 0.f;
+    const int64_t b = seq_start / seq_len;
+    return ld_any(halo, halo_dt, b * hs0 + d * hs1 + (halo_S - m) * hs2);
+  }
   // Rows per item (upper bound).
   __host__ __device__ int32_t item_rows() const { return varlen ? chunk_size : tile; }
 
@@ -148,6 +164,14 @@ inline RowMap make_rowmap(const moc_problem& p, int32_t fixed_tile) {
     m.seq_len = p.seq_len;
     m.tile = fixed_tile;
     m.tiles_per_seq = (p.seq_len + fixed_tile - 1) / fixed_tile;
+    if (p.halo != nullptr) {
+      m.halo = p.halo;
+      m.hs0 = p.halo_strides[0];
+      m.hs1 = p.halo_strides[1];
+      m.hs2 = p.halo_strides[2];
+      m.halo_S = p.kernel_size;
+      m.halo_dt = p.x_dtype;
+    }
   }
   return m;
 }

@@ -54,7 +54,7 @@ __device__ __forceinline__ float conv_pre(const ConvArgs<XT>& a, int64_t r, int6
       const float bv = cround<BF>(ld_any(a.basis, a.bdt, (static_cast<int64_t>(k) * a.S + s) * a.D + d));
       w = fmaf(av, bv, w);
     }
-    const float xv = src >= seq_start ? to_f32(a.x[src * a.D + d]) : 0.f;
+    const float xv = src >= seq_start ? to_f32(a.x[src * a.D + d]) : a.rm.halo_at(seq_start, src, d);
     acc = fmaf(xv, w, acc);
   }
   return acc;
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(256) k_dalpha(ConvArgs<XT> a) {
       const float g = dz_at(a, r, d);
       for (int s = 0; s < a.S; ++s) {
         const int64_t src = r - (a.S - 1 - s);
-        const float xv = src >= ss ? to_f32(a.x[src * a.D + d]) : 0.f;
+        const float xv = src >= ss ? to_f32(a.x[src * a.D + d]) : a.rm.halo_at(ss, src, d);
         const float m = cround<BF>(g * xv);
 #pragma unroll
         for (int k = 0; k < KMAX; ++k) {
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(256) k_dbasis_partial(ConvArgs<XT> a) {
       if (!a.rm.item(i, ss, se, r0, r1)) continue;
       for (int64_t r = r0; r < r1; ++r) {
         const int64_t src = r - (a.S - 1 - s);
-        const float xv = src >= ss ? to_f32(a.x[src * a.D + d]) : 0.f;
+        const float xv = src >= ss ? to_f32(a.x[src * a.D + d]) : a.rm.halo_at(ss, src, d);
         const float m = cround<BF>(dz_at(a, r, d) * xv);
         acc = fmaf(cround<BF>(ld_any(a.alpha, a.adt, r * a.K + k)), m, acc);
       }

@@ -158,6 +158,22 @@ __device__ __forceinline__ void zero_rows(char* stage, int zx, int zdy) {
   }
 }
 
+// Fills the x-tile rows of the tokens ss-1 .. ss-(S-1) before the sequence from the
+// attached cache (prefill with a cache); called after zero_rows, between CTA barriers.
+template <class L>
+__device__ __forceinline__ void fill_halo(char* stage, const RowMap& rm, int64_t ss, int64_t r0, int64_t ch_base,
+                                          int64_t D, int S) {
+  for (int idx = threadIdx.x; idx < (S - 1) * kBD; idx += kThreads) {
+    const int m = idx / kBD + 1, ch = idx - (m - 1) * kBD;
+    const int64_t row = ss - m - (r0 - kHalo);
+    const int64_t gch = ch_base + ch;
+    if (row < 0 || row >= L::XR || gch >= D) continue;
+    const int r = static_cast<int>(row), c64 = ch & 63;
+    *reinterpret_cast<bf16*>(stage + (ch >> 6) * L::xbox + r * 128 + ((((c64 >> 3) ^ r) & 7) << 4) + (c64 & 7) * 2) =
+        __float2bfloat16_rn(rm.halo_at(ss, ss - m, gch));
+  }
+}
+
 // ------------------------------------------------------------------ forward
 
 template <int KT, int S, bool ACT>
@@ -239,6 +255,10 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
       if (zx > 0) {  // uniform across the CTA
         zero_rows<L>(stage_p, zx, L::FR);
         __syncthreads();
+        if (a.rm.halo != nullptr) {
+          fill_halo<L>(stage_p, a.rm, ss, r0, ch_base, a.D, S);
+          __syncthreads();
+        }
       }
       const uint32_t x_s = sm.stages + cur * L::stage_bytes;
       const uint32_t a_s = x_s + L::x_bytes;
@@ -404,6 +424,10 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
       if (zx > 0 || zdy < L::FR) {  // uniform across the CTA
         zero_rows<L>(stage_p, zx, zdy);
         __syncthreads();
+        if (zx > 0 && a.rm.halo != nullptr) {
+          fill_halo<L>(stage_p, a.rm, ss, r0, ch_base, a.D, S);
+          __syncthreads();
+        }
       }
     }
 

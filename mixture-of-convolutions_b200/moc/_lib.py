@@ -43,6 +43,8 @@ class MocProblem(ctypes.Structure):
         ("chunk_indices_dtype", ctypes.c_int32),
         ("n_chunks", ctypes.c_int64),
         ("chunk_size", ctypes.c_int32),
+        ("halo", ctypes.c_void_p),
+        ("halo_strides", ctypes.c_int64 * 3),
     ]
 
 

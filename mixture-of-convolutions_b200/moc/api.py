@@ -134,6 +134,7 @@ class _MoCFunction(torch.autograd.Function):
         max_seqlen: Optional[int],
         cu_seqlens_cpu: Optional[torch.Tensor],
         chunk_indices: Optional[torch.Tensor],
+        halo: Optional[torch.Tensor] = None,
     ) -> torch.Tensor:
         x, alpha, basis = x.contiguous(), alpha.contiguous(), basis.contiguous()
         varlen = cu_seqlens is not None
@@ -157,13 +158,14 @@ class _MoCFunction(torch.autograd.Function):
 
         act = activation_flag(activation)
         out = ops.launch_forward(
-            x, alpha, basis, activation_flag=act, cu_seqlens=cu_seqlens, chunk_indices=chunk_indices,
+            x, alpha, basis, activation_flag=act, cu_seqlens=cu_seqlens, chunk_indices=chunk_indices, halo=halo,
         )
         saved = (x, alpha, basis, cu_seqlens) if varlen else (x, alpha, basis)
         ctx.save_for_backward(*saved)
         ctx.activation_flag = act
         ctx.is_varlen = varlen
         ctx.chunk_indices = chunk_indices
+        ctx.halo = halo
         return out
 
     @staticmethod
@@ -180,8 +182,9 @@ class _MoCFunction(torch.autograd.Function):
             need_x=ctx.needs_input_grad[0],
             cu_seqlens=cu_seqlens,
             chunk_indices=ctx.chunk_indices,
+            halo=ctx.halo,
         )
-        return dx, dalpha, dbasis, None, None, None, None, None
+        return dx, dalpha, dbasis, None, None, None, None, None, None
 
 
 class _RouterFunction(torch.autograd.Function):
@@ -306,11 +309,16 @@ def moc_triton(
             if T == 1:
                 y = _step_moc(x, alpha, basis, cache, activation)
                 return y, (cache if output_final_state else None)
-            prefix_x = cache.transpose(1, 2)
-            prefix_alpha = alpha.new_zeros(B, KS, K)
-            y = _fixed_moc(
-                torch.cat((prefix_x, x), dim=1), torch.cat((prefix_alpha, alpha), dim=1), basis, activation,
-            )[:, KS:]
+            if cache.requires_grad and torch.is_grad_enabled():
+                # the reference's form, which also differentiates the cache
+                prefix_x = cache.transpose(1, 2)
+                prefix_alpha = alpha.new_zeros(B, KS, K)
+                y = _fixed_moc(
+                    torch.cat((prefix_x, x), dim=1), torch.cat((prefix_alpha, alpha), dim=1), basis, activation,
+                )[:, KS:]
+            else:
+                # the kernels read the cache as the sequences' causal halo (no concatenation)
+                y = _MoCFunction.apply(x, alpha, basis, activation, None, None, None, None, cache.detach())
         else:
             y = _fixed_moc(x, alpha, basis, activation)
         return y, (_final_state(x, cache, KS) if output_final_state else None)

@@ -129,6 +129,7 @@ def _problem(
     cu_seqlens_cpu: torch.Tensor | None,
     chunk_indices: torch.Tensor | None,
     block_t: int,
+    halo: torch.Tensor | None = None,
 ) -> tuple[_lib.MocProblem, tuple]:
     """Fill a moc_problem; returns it with the tensors that must outlive the call."""
     K, S, D = basis.shape
@@ -162,6 +163,13 @@ def _problem(
         p.batch = B
         p.seq_len = T
         p.n_tokens = B * T
+        if halo is not None:
+            if halo.shape != (B, D, S) or halo.dtype != x.dtype or halo.device != x.device:
+                raise ValueError(f"halo must be a [{B}, {D}, {S}] {x.dtype} tensor on x's device")
+            p.halo = _lib.ptr(halo)
+            for i, st in enumerate(halo.stride()):
+                p.halo_strides[i] = st
+            keep = (halo,)
     return p, keep
 
 
@@ -175,11 +183,15 @@ def launch_forward(
     cu_seqlens_cpu: torch.Tensor | None = None,
     chunk_indices: torch.Tensor | None = None,
     block_t: int = VARLEN_BLOCK_T,
+    halo: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """y = [silu](conv(x, alpha, basis)) in x.dtype (reference: moc/ops.py:129-194)."""
+    """y = [silu](conv(x, alpha, basis)) in x.dtype (reference: moc/ops.py:129-194).
+
+    ``halo`` (an extension, fixed length only): the conv cache [B, D, S] of the tokens
+    before each sequence, read by the first S-1 positions' taps instead of zeros."""
     x, alpha, basis = _aligned(x), _aligned(alpha), _aligned(basis)
     out = torch.empty_like(x)
-    p, keep = _problem(x, alpha, basis, activation_flag, cu_seqlens, cu_seqlens_cpu, chunk_indices, block_t)
+    p, keep = _problem(x, alpha, basis, activation_flag, cu_seqlens, cu_seqlens_cpu, chunk_indices, block_t, halo)
     with torch.cuda.device(x.device):
         rc = _lib.load().moc_forward(
             ctypes.byref(p), _lib.ptr(x), _lib.ptr(alpha), _lib.ptr(basis), _lib.ptr(out),
@@ -220,16 +232,18 @@ def launch_backward(
     cu_seqlens_cpu: torch.Tensor | None = None,
     chunk_indices: torch.Tensor | None = None,
     block_t: int = VARLEN_BLOCK_T,
+    halo: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor | None, torch.Tensor, torch.Tensor]:
     """(dx | None, dalpha, dbasis) (reference: moc/ops.py:216-338).
 
     With ``activation_flag`` set the kernels recompute the pre-activation on chip in
     fp32, so ``preact`` is accepted for signature compatibility but not read.  dbasis
     is reduced deterministically (per-CTA fp32 partials summed in a fixed order).
+    ``halo`` as in launch_forward (the cache gets no gradient).
     """
     del preact
     x, alpha, basis, moc_dy = _aligned(x), _aligned(alpha), _aligned(basis), _aligned(moc_dy)
-    p, keep = _problem(x, alpha, basis, activation_flag, cu_seqlens, cu_seqlens_cpu, chunk_indices, block_t)
+    p, keep = _problem(x, alpha, basis, activation_flag, cu_seqlens, cu_seqlens_cpu, chunk_indices, block_t, halo)
     lib = _lib.load()
     dx = torch.empty_like(x) if need_x else None
     dalpha = torch.empty_like(alpha)

@@ -227,10 +227,50 @@ def test_prefill_continuation_with_cache(xdt):
     assert torch.equal(state2, kx[:, -S:].transpose(1, 2))
 
 
+@pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float32], ids=["bf16", "fp32"])
+@pytest.mark.parametrize("S,act", [(4, None), (3, "silu"), (2, None), (1, "silu")])
+def test_prefill_with_cache_reads_the_cache_as_halo(kernel_path, xdt, S, act):
+    """A cache with T > 1: the kernels read the cache as each sequence's causal halo.  y and
+    the gradients of x, alpha and basis equal the reference's form (cache prepended with
+    zero routing weights, moc/api.py:299-309) in the float64 oracle, and the GPU result of
+    that form (taken when the cache needs a gradient)."""
+    B, T, D, K = 2, 70, 192, 16
+    g = torch.Generator().manual_seed(30 + S)
+    x = torch.randn(B, T, D, generator=g) * 0.5
+    a = torch.softmax(torch.randn(B, T, K, generator=g), dim=-1)
+    basis = torch.randn(K, S, D, generator=g) * 0.2
+    cache = torch.randn(B, D, S, generator=g) * 0.5
+    dy = torch.randn(B, T, D, generator=g) * 0.1
+    # oracle of the prepended form, rows t >= 0
+    px = torch.cat((cache.to(xdt).double().transpose(1, 2), x.to(xdt).double()), 1)
+    pa = torch.cat((torch.zeros(B, S, K, dtype=torch.float64), a.to(xdt).double()), 1)
+    pdy = torch.cat((torch.zeros(B, S, D, dtype=torch.float64), dy.to(xdt).double()), 1)
+    ref = O.conv_grads(px, pa, basis.to(xdt).double(), pdy, activation=act)
+    ref = {"y": ref["y"][:, S:], "dx": ref["dx"][:, S:], "dalpha": ref["dalpha"][:, S:], "dbasis": ref["dbasis"]}
+    kx = x.to(xdt).cuda().requires_grad_()
+    ka = a.to(xdt).cuda().requires_grad_()
+    kb = basis.to(xdt).cuda().requires_grad_()
+    kc = cache.to(xdt).cuda().transpose(1, 2).contiguous().transpose(1, 2)  # a strided [B, D, S] view
+    y, _ = moc_triton(kx, ka, kb, cache=kc, activation=act)
+    y.backward(dy.to(xdt).cuda())
+    got = {"y": y, "dx": kx.grad, "dalpha": ka.grad, "dbasis": kb.grad}
+    _assert_close(got, ref, xdt, f"prefill S={S} {act}")
+    # the reference's form on the GPU (cache with requires_grad) agrees as well
+    kx2, ka2, kb2 = (t.detach().clone().requires_grad_() for t in (kx, ka, kb))
+    kc2 = kc.detach().clone().requires_grad_()
+    y2, _ = moc_triton(kx2, ka2, kb2, cache=kc2, activation=act)
+    y2.backward(dy.to(xdt).cuda())
+    for name, t1, t2 in (("y", y, y2), ("dx", kx.grad, kx2.grad), ("dalpha", ka.grad, ka2.grad),
+                         ("dbasis", kb.grad, kb2.grad)):
+        assert rel_err(t1, t2) <= max(TOL[xdt], STORE_TOL[t1.dtype]), name
+    assert kc2.grad is not None
+
+
 # ------------------------------------------------------------- larger shapes
 
 @pytest.mark.parametrize("B,T,D,K,S", [(2, 300, 520, 16, 4), (1, 130, 256, 32, 8), (3, 77, 192, 4, 3),
-                                       (1, 64, 2048, 16, 4)])
+                                       (1, 64, 2048, 16, 4), (3, 333, 384, 16, 4), (2, 256, 2048, 8, 2),
+                                       (1, 129, 96, 16, 3), (2, 200, 160, 16, 1)])
 def test_larger_shapes_bf16(kernel_path, B, T, D, K, S):
     x, a, dy, basis = _inputs(B, T, D, K, S, seed=7)
     got, ref = _run(x, a, basis, dy, torch.bfloat16, torch.bfloat16, torch.bfloat16, "silu")
