@@ -136,6 +136,25 @@ class NVLinkGradAllReduce:
         with torch.cuda.device(dev):
             rc = lib.moc_comm_connect(comm, blob)
         self._agree(rc == _lib.MOC_OK, "moc_comm_connect", rc, group)
+        self._self_check(group)
+
+    def _self_check(self, group) -> None:
+        """One sum of a probe buffer checked against torch.distributed's all-reduce, agreed
+        over `group` (so a peer path that does not work raises on every rank)."""
+        g = torch.Generator(device=self.device).manual_seed(1000 + dist.get_rank(group))
+        probe = torch.randn(sum(p.numel() for p in self.params), generator=g, device=self.device)
+        ref = probe.clone()
+        dist.all_reduce(ref, group=group)
+        segs, off = [], 0
+        for p in self.params:
+            segs.append(probe.narrow(0, off, p.numel()))
+            off += p.numel()
+        _lib.device_status(clear=True)
+        self(segs)
+        torch.cuda.synchronize(self.device)
+        ok = _lib.device_status(clear=True) == 0 and bool(
+            torch.allclose(probe, ref, rtol=1e-5, atol=1e-5 * float(ref.abs().max())))
+        self._agree(ok, "the NVLink all-reduce self-check", _lib.MOC_OK, group)
 
     def _agree(self, ok: bool, what: str, rc: int, group) -> None:
         flag = torch.tensor([1 if ok else 0], dtype=torch.int32)
@@ -147,6 +166,7 @@ class NVLinkGradAllReduce:
         self.close(sync=False)
         if not ok:
             _lib.check(rc, what)
+            raise RuntimeError(f"{what} failed on this rank")
         raise RuntimeError(f"{what} failed on another rank")
 
     def __call__(self, grads: Sequence[torch.Tensor] | None = None) -> list[torch.Tensor]:
