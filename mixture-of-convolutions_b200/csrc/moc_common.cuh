@@ -94,6 +94,7 @@ struct RowMap {
   int64_t batch = 0, seq_len = 0, n_tokens = 0;
   int64_t tiles_per_seq = 0;
   int32_t tile = 0;
+  int32_t idx32 = 0;  // fixed length with fewer than 2^31 items: item() divides in 32 bits
   int32_t varlen = 0;
   const void* cu = nullptr;
   int32_t cu_i64 = 0;
@@ -126,8 +127,16 @@ struct RowMap {
   __device__ __forceinline__ bool item(int64_t i, int64_t& seq_start, int64_t& seq_end, int64_t& r0,
                                        int64_t& r1) const {
     if (!varlen) {
-      const int64_t b = i / tiles_per_seq;
-      const int64_t c = i - b * tiles_per_seq;
+      int64_t b, c;
+      if (idx32) {  // 32-bit division: a 64-bit one is a long subroutine on the GPU
+        const uint32_t ii = static_cast<uint32_t>(i), tps = static_cast<uint32_t>(tiles_per_seq);
+        const uint32_t b32 = ii / tps;
+        b = b32;
+        c = ii - b32 * tps;
+      } else {
+        b = i / tiles_per_seq;
+        c = i - b * tiles_per_seq;
+      }
       seq_start = b * seq_len;
       seq_end = seq_start + seq_len;
       r0 = seq_start + c * tile;
@@ -164,6 +173,7 @@ inline RowMap make_rowmap(const moc_problem& p, int32_t fixed_tile) {
     m.seq_len = p.seq_len;
     m.tile = fixed_tile;
     m.tiles_per_seq = (p.seq_len + fixed_tile - 1) / fixed_tile;
+    m.idx32 = p.batch * m.tiles_per_seq < (int64_t{1} << 31) ? 1 : 0;
     if (p.halo != nullptr) {
       m.halo = p.halo;
       m.hs0 = p.halo_strides[0];
