@@ -376,6 +376,96 @@ def run_decode(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
+def varlen_lengths(total: int, seed: int) -> list[int]:
+    """Config 3 sequence lengths: uniform in [64, 4096] from a seeded generator, the last
+    one truncated so that they add up to `total`."""
+    g = torch.Generator().manual_seed(seed)
+    lens, acc = [], 0
+    while acc < total:
+        n = int(torch.randint(64, 4097, (1,), generator=g))
+        n = min(n, total - acc)
+        lens.append(n)
+        acc += n
+    return lens
+
+
+def run_varlen(args, rank: int, world: int, local_rank: int) -> None:
+    """Config 3: 16384 packed tokens of sequences with lengths uniform in [64, 4096], D=Dz=2048,
+    K=16, S=4, exp router, fused SiLU; one MoC fwd+bwd per step, captured in a CUDA graph.
+    Each rank runs its own packed batch (weak scaling, no collective: replicas)."""
+    from moc import MoC, _lib
+    import moc.ops as ops
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
+    total, D, K, S = 16384, 2048, 16, 4
+    lens = varlen_lengths(total, 31 + rank)
+    cu_cpu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32)
+    cu = cu_cpu.to(device)
+    chunks = ops.prepare_chunk_indices(cu, cu_seqlens_cpu=cu_cpu)
+    torch.manual_seed(1234)
+    m = MoC(dim=D, z_dim=D, kernel_size=S, k=K, activation="silu", init_std=0.002, router_activation="exp")
+    with torch.no_grad():
+        m.router.copy_(torch.randn(K, D, generator=torch.Generator().manual_seed(4321)) * 0.02)
+    m = m.to(device=device, dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(99 + rank)
+    x = torch.randn(1, total, D, generator=g).bfloat16().to(device).requires_grad_()
+    z = torch.randn(1, total, D, generator=g).bfloat16().to(device).requires_grad_()
+    dy = torch.randn(1, total, D, generator=g).bfloat16().to(device)
+    maxlen = max(lens)
+
+    def step():
+        y, _ = m(x, z, cu_seqlens=cu, max_seqlen=maxlen, chunk_indices=chunks)
+        return torch.autograd.grad(y, (x, z, m.conv_bases, m.router), dy)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    l0 = _lib.launch_count()
+    step()
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - l0
+    stream = torch.cuda.current_stream(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    sampler = ClockSampler(device, os.environ.get("TMPDIR", "/tmp"))
+    barrier(world)
+    t0 = time.time()
+    ms = time_region(graph.replay, args.steps, stream)
+    t1 = time.time()
+    barrier(world)
+    ms = max_over_ranks(ms, world)
+    clocks = sampler.summary(t0, t1)
+    nbytes = step_bytes_per_token(D, D, K) * total
+    peaks = measured_peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "MoC varlen fwd+bwd tokens/s", "value": total * world / (ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "config3: packed varlen MoC fwd+bwd, 16384 tokens, lengths U[64,4096], "
+                                   "D=z_dim=2048, K=16, S=4, exp router, SiLU",
+                       "n_seqs": len(lens), "parallelism": f"replicas{world}",
+                       "timing": "CUDA graph of one step replayed K times; CUDA events"},
+            "roofline": {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                         "algorithmic_bytes_per_step": nbytes},
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks,
+        }), flush=True)
+    sampler.stop()
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def bench_config(cfg: dict, world: int) -> dict:
     """The workload description both arms print."""
     return {"workload": "config2: MoC module fwd+bwd, B=4 T=4096 D=z_dim=2048 K=16 S=4 bf16 softmax",
@@ -413,8 +503,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("train", "decode"), default="train",
-                    help="train: config 2 (the headline); decode: config 4, three modules, batch 128")
+    ap.add_argument("--workload", choices=("train", "decode", "varlen"), default="train",
+                    help="train: config 2 (the headline); decode: config 4, three modules, batch 128; "
+                         "varlen: config 3, packed sequences, exp router, SiLU")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -427,6 +518,9 @@ def main() -> None:
         return
     if args.workload == "decode":
         run_decode(args, rank, world, local_rank)
+        return
+    if args.workload == "varlen":
+        run_varlen(args, rank, world, local_rank)
         return
 
     from moc import _lib, dp

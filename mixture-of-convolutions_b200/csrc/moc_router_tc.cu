@@ -363,23 +363,13 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
   }
 }
 
-// dweight[i] = sum over token groups of the partials, in group order; thread = 4
-// consecutive outputs (K * Dz is a multiple of 4 here: Dz % 8 == 0), one 16-byte load per
-// group, all in flight together.
-__global__ void __launch_bounds__(256) k_sum_groups(const float* __restrict__ part, int64_t groups, int64_t n, void* out,
-                                                    int dtype) {
-  for (int64_t i4 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i4 < n / 4;
-       i4 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+__global__ void k_sum_groups(const float* __restrict__ part, int64_t groups, int64_t n, void* out, int dtype) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float s = 0.f;
 #pragma unroll 8
-    for (int64_t g = 0; g < groups; ++g) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(part + g * n) + i4);
-      s.x += v.x, s.y += v.y, s.z += v.z, s.w += v.w;
-    }
-    st_any(out, dtype, 4 * i4, s.x);
-    st_any(out, dtype, 4 * i4 + 1, s.y);
-    st_any(out, dtype, 4 * i4 + 2, s.z);
-    st_any(out, dtype, 4 * i4 + 3, s.w);
+    for (int64_t g = 0; g < groups; ++g) s += __ldg(part + g * n + i);
+    st_any(out, dtype, i, s);
   }
 }
 
@@ -444,7 +434,7 @@ int bwd_kt(RouterBwdArgs& a, const void* z, int64_t slices, int64_t groups, void
   note_launch();
   if (dw != nullptr) {
     const int64_t n = static_cast<int64_t>(a.K) * a.Dz;
-    const int64_t blocks = std::min<int64_t>(ceil_div(n / 4, 256), 4 * sm_count_r());
+    const int64_t blocks = std::min<int64_t>(ceil_div(n, 256), 4 * sm_count_r());
     k_sum_groups<<<static_cast<unsigned>(blocks), 256, 0, st>>>(a.dw_part, groups, n, dw, MOC_DTYPE_BF16);
     note_launch();
   }

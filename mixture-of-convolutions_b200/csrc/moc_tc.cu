@@ -642,31 +642,23 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
 }
 
 // dalpha[i] = sum over channel slices, dbasis[i] = sum over token groups (fixed order).
-// Thread = 4 consecutive outputs: every partial row is one 16-byte load, all of them in
-// flight together (nk and ksd are multiples of 4 on this path: K % 8 == 0, D % 8 == 0).
-__global__ void __launch_bounds__(256) k_tc_finalize(const float* __restrict__ da_part, int64_t n_slices, int64_t nk,
-                                                     void* dalpha, int adt, const float* __restrict__ db_part,
-                                                     int64_t groups, int64_t ksd, void* dbasis, int bdt) {
-  const int64_t n4 = (nk + ksd) / 4;
-  for (int64_t i4 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i4 < n4;
-       i4 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t i = 4 * i4;
-    const bool da = i < nk;
-    const float* src = da ? da_part + i : db_part + (i - nk);
-    const int64_t stride = da ? nk : ksd, count = da ? n_slices : groups;
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+__global__ void k_tc_finalize(const float* __restrict__ da_part, int64_t n_slices, int64_t nk, void* dalpha,
+                              int adt, const float* __restrict__ db_part, int64_t groups, int64_t ksd, void* dbasis,
+                              int bdt) {
+  const int64_t total = nk + ksd;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float s = 0.f;
+    if (i < nk) {
 #pragma unroll 8
-    for (int64_t c = 0; c < count; ++c) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(src + c * stride));
-      s.x += v.x, s.y += v.y, s.z += v.z, s.w += v.w;
+      for (int64_t c = 0; c < n_slices; ++c) s += __ldg(da_part + c * nk + i);
+      st_any(dalpha, adt, i, s);
+    } else {
+      const int64_t j = i - nk;
+#pragma unroll 8
+      for (int64_t g = 0; g < groups; ++g) s += __ldg(db_part + g * ksd + j);
+      st_any(dbasis, bdt, j, s);
     }
-    void* dst = da ? dalpha : dbasis;
-    const int dt = da ? adt : bdt;
-    const int64_t o = da ? i : i - nk;
-    st_any(dst, dt, o, s.x);
-    st_any(dst, dt, o + 1, s.y);
-    st_any(dst, dt, o + 2, s.z);
-    st_any(dst, dt, o + 3, s.w);
   }
 }
 
@@ -766,7 +758,7 @@ int bwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alph
   note_launch();
   rc = note_cuda(cudaGetLastError());
   if (rc != MOC_OK) return rc;
-  const int64_t blocks = std::min<int64_t>(ceil_div((nk + ksd) / 4, 256), 8 * sm_count());
+  const int64_t blocks = std::min<int64_t>(ceil_div(nk + ksd, 256), 8 * sm_count());
   k_tc_finalize<<<static_cast<unsigned>(blocks), 256, 0, st>>>(args.da_part, pl.slices, nk, dalpha, p.alpha_dtype,
                                                                args.db_part, pl.groups, ksd, dbasis, p.basis_dtype);
   note_launch();
