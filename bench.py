@@ -43,6 +43,10 @@ import torch.distributed as dist  # noqa: E402
 
 CONFIG = {"B": 4, "T": 4096, "D": 2048, "Dz": 2048, "K": 16, "S": 4, "router": "softmax", "activation": None,
           "init_std": 0.002, "router_std": 0.02}
+# config 5, per rank: the large data-parallel case (B=32 over 8 GPUs, so 4 sequences per GPU),
+# bases at the fan-in std sqrt(K / (3 S))
+CONFIG_LARGE = {"B": 4, "T": 8192, "D": 4096, "Dz": 4096, "K": 32, "S": 8, "router": "softmax", "activation": None,
+                "init_std": (32 / (3 * 8)) ** 0.5, "router_std": 0.02}
 METRIC = "MoC fwd+bwd tokens/s"
 FALLBACK_HBM_GBS = 6650.0
 
@@ -468,18 +472,24 @@ def run_varlen(args, rank: int, world: int, local_rank: int) -> None:
 
 def bench_config(cfg: dict, world: int) -> dict:
     """The workload description both arms print."""
-    return {"workload": "config2: MoC module fwd+bwd, B=4 T=4096 D=z_dim=2048 K=16 S=4 bf16 softmax",
+    if cfg["D"] == CONFIG_LARGE["D"]:
+        name = (f"config5: large data-parallel MoC fwd+bwd, B=4 per GPU (B={4 * world} over {world}), T=8192, "
+                "D=z_dim=4096 K=32 S=8 bf16 softmax, fan-in init")
+    else:
+        name = "config2: MoC module fwd+bwd, B=4 T=4096 D=z_dim=2048 K=16 S=4 bf16 softmax"
+    in_mib = 3 * cfg["B"] * cfg["T"] * cfg["D"] * 2 // (1 << 20)
+    return {"workload": name,
             "global_batch": cfg["B"] * world, "seq_len": cfg["T"], "D": cfg["D"], "z_dim": cfg["Dz"],
             "K": cfg["K"], "S": cfg["S"], "parallelism": f"dp{world}",
-            "l2": "inputs larger than L2 (x, z, dy = 192 MiB per rank)",
+            "l2": f"inputs larger than L2 (x, z, dy = {in_mib} MiB per rank)",
             "timing": "CUDA graph of one step replayed K times; CUDA events; max over ranks"}
 
 
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    cfg = dict(CONFIG)
-    seq = 2048
+    cfg = dict(CONFIG_LARGE if args.workload == "large" else CONFIG)
+    seq = 1024 if args.workload == "large" else 2048
     base = cpu_baseline(cfg, iters=max(1, min(args.steps, 3)), seq_tokens=seq)
     line = {
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus,
@@ -503,9 +513,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("train", "decode", "varlen"), default="train",
+    ap.add_argument("--workload", choices=("train", "decode", "varlen", "large"), default="train",
                     help="train: config 2 (the headline); decode: config 4, three modules, batch 128; "
-                         "varlen: config 3, packed sequences, exp router, SiLU")
+                         "varlen: config 3, packed sequences, exp router, SiLU; large: config 5, "
+                         "4 sequences of 8192 tokens per GPU, D=4096, K=32, S=8")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -529,7 +540,7 @@ def main() -> None:
     device = torch.device("cuda", local_rank)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
-    cfg = dict(CONFIG)
+    cfg = dict(CONFIG_LARGE if args.workload == "large" else CONFIG)
     N_rank = cfg["B"] * cfg["T"]
 
     m, host = make_module_and_inputs(cfg, rank, device)
@@ -653,7 +664,7 @@ def main() -> None:
     peaks = measured_peaks()
     kbytes = KERNEL_BYTES_PER_TOKEN[dominant](cfg) * N_rank
     achieved = kbytes / (kernel_ms[dominant] * 1e-3) / 1e9
-    traffic = profiled_traffic(dominant)
+    traffic = profiled_traffic(dominant if args.workload == "train" else f"{args.workload}:{dominant}")
 
     step_bytes = step_bytes_per_token(cfg["D"], cfg["Dz"], cfg["K"]) * N_rank
     tokens_all = N_rank * world
@@ -691,7 +702,7 @@ def main() -> None:
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
-            base = cpu_baseline(cfg)
+            base = cpu_baseline(cfg, seq_tokens=1024 if args.workload == "large" else 2048)
             line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
 

@@ -66,6 +66,17 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64
     g_last_cuda_error = "cuTensorMapEncodeTiled entry point unavailable";
     return MOC_ERR_CUDA;
   }
+  // The encoding is a driver call and needs a current context on this thread.  A thread
+  // that has made no runtime call of this library yet (the autograd engine's device
+  // thread, say) may have none: bind the device's primary context once per thread.
+  thread_local uint64_t bound = 0;
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce == cudaSuccess && dev >= 0 && dev < 64 && !((bound >> dev) & 1)) {
+    ce = cudaSetDevice(dev);
+    if (ce == cudaSuccess) bound |= uint64_t{1} << dev;
+  }
+  if (ce != cudaSuccess) return note_cuda(ce);
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_bytes};
   const cuuint32_t box[2] = {box_inner, box_outer};

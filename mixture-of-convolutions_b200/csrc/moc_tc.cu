@@ -41,11 +41,20 @@ constexpr int kFut = 16;               // future rows kept after each tile (S - 
 
 constexpr int align1k(int v) { return (v + 1023) / 1024 * 1024; }
 
-template <int KT, int S, bool ACT, bool BWD>
+// PART (backward only) selects the work of one launch: kBwdAll (dx, dalpha and dbasis in
+// one pass), or, where the dbasis accumulators (S x KP x 16 channels per warp) would leave
+// no registers for anything else, two passes: kBwdDxDa (dx, dalpha) and kBwdDb (dbasis).
+constexpr int kBwdAll = 0, kBwdDxDa = 1, kBwdDb = 2;
+constexpr bool bwd_split(int KT, int S) { return KT * S > 8; }
+
+template <int KT, int S, bool ACT, bool BWD, int PART = kBwdAll>
 struct Layout {
   static constexpr int KP = KT * 16;  // bases padded to the MMA K
-  // basis fragments live in registers when they fit (<= 4 (tap, 16-base) groups)
-  static constexpr bool BREG = KT * S <= 4;
+  // basis fragments live in registers where they fit beside the accumulators (<= 4 (tap,
+  // 16-base) groups), and in the dx / dalpha pass of a split backward (no dbasis
+  // accumulators, one CTA per SM by shared memory either way), where reading them from
+  // shared memory every tap would bound the pass
+  static constexpr bool BREG = KT * S <= 4 || PART == kBwdDxDa;
   static constexpr int XR = kHalo + kTile + ((BWD && ACT) ? kFut : 0);  // x rows per stage
   // rows of dy / alpha after the tile start: the dx taps read up to S-1 <= 7 future rows;
   // with SiLU the pre-activation of those rows is one more 16-row MMA block.
@@ -61,8 +70,9 @@ struct Layout {
   static constexpr int tx_bytes = x_bytes + dy_bytes + AR * ARB;
   static constexpr int basis_bytes = S * KP * kRowB;
   // dalpha partials of RB 16-row blocks x 8 warps, reduced across warps once per RB blocks
-  static constexpr int RB = KT == 1 ? 4 : 2;
-  static constexpr int red_bytes = BWD ? RB * 8 * 16 * KP * 4 : 0;
+  // (with the basis staged beside them at 32 bases and more than 4 taps: one block)
+  static constexpr int RB = (KT == 1 || BREG) ? 4 : (S > 4 ? 1 : 2);
+  static constexpr int red_bytes = (BWD && PART != kBwdDb) ? RB * 8 * 16 * KP * 4 : 0;
   // with register-resident basis fragments the basis staging area is reused for the
   // dalpha reduction buffer once the fragments are loaded
   static constexpr int head_bytes =
@@ -71,7 +81,10 @@ struct Layout {
   // per-warp output staging: one 16-row x 16-channel bf16 block (32-byte rows)
   static constexpr int ost_bytes = BWD ? 0 : 8 * 16 * 32;
   static constexpr int total = 1024 + 2 * stage_bytes + head_bytes + dz_bytes + ost_bytes + 64;
-  static constexpr int min_blocks = BWD ? ((BREG && !ACT && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 3 : 2);
+  // forward at 32 bases and more than 4 taps: its 68 KB basis staging leaves room for at
+  // most two CTAs anyway, and the 64 basis fragment registers need more than 128 per thread
+  static constexpr int min_blocks =
+      BWD ? ((BREG && !ACT && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 3 : (KT * S > 8 ? 1 : 2));
 };
 
 struct TcArgs {
@@ -183,7 +196,6 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
   extern __shared__ __align__(1024) char smem_raw[];
   const Smem<L> sm(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, q = lane & 3;
   const int64_t ch_base = static_cast<int64_t>(blockIdx.x) * kBD;
   const int64_t n_items = a.rm.n_items();
   const int64_t i0 = static_cast<int64_t>(blockIdx.y) * a.items_per_group;
@@ -320,17 +332,19 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
 
 // ------------------------------------------------------------------ backward
 
-template <int KT, int S, bool ACT>
-__global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_blocks))
+template <int KT, int S, bool ACT, int PART>
+__global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min_blocks))
     k_tc_bwd(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap dymap,
              const __grid_constant__ CUtensorMap amap, TcArgs a) {
-  using L = Layout<KT, S, ACT, true>;
+  using L = Layout<KT, S, ACT, true, PART>;
   constexpr int KP = L::KP;
   constexpr bool BREG = L::BREG;
+  constexpr bool DXDA = PART != kBwdDb;  // this launch computes dx and dalpha
+  constexpr bool DB = PART != kBwdDxDa;  // this launch computes dbasis
   extern __shared__ __align__(1024) char smem_raw[];
   const Smem<L> sm(smem_raw);
   char* basis_s = sm.head;
-  float* red_s = reinterpret_cast<float*>(sm.head + (BREG ? 0 : L::basis_bytes));  // [2][8 warps][16][KP]
+  float* red_s = reinterpret_cast<float*>(sm.head + (BREG ? 0 : L::basis_bytes));  // [RB][8 warps][16][KP]
   char* dz_s = sm.dz;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
@@ -339,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
   const int64_t n_items = a.rm.n_items();
   const int64_t i0 = static_cast<int64_t>(blockIdx.y) * a.items_per_group;
   const int64_t i1 = i0 + a.items_per_group < n_items ? i0 + a.items_per_group : n_items;
-  const bool want_dx = a.dx != nullptr;
+  const bool want_dx = DXDA && a.dx != nullptr;
   const int ch_w = warp * 16;  // this warp's channel offset inside the slice
 
   // per-lane constants: basis rows (padded, unswizzled), alpha rows (dense), and the
@@ -354,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
   const uint32_t dy_box = static_cast<uint32_t>(L::x_bytes + (warp >> 2) * L::dybox);
   const int m_chunk = 2 * (warp & 3) + (lane >> 4);
 
-  float dba[S][2 * KT][4] = {};      // dbasis^T accumulators: (ch g | g+8) x (k 8kn + 2q..)
+  float dba[DB ? S : 1][2 * KT][4] = {};  // dbasis^T accumulators: (ch g | g+8) x (k 8kn + 2q..)
   uint32_t bw[BREG ? S : 1][KT][4];  // basis, B operand of W = alpha . basis_s
   uint32_t bd[BREG ? S : 1][KT][4];  // basis^T, B operand of dalpha = m . basis_s^T
 
@@ -518,9 +532,11 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
     const int nb = (rows + 15) >> 4;  // uniform across the CTA
 #pragma unroll 1
     for (int b = 0; b < nb; ++b) {
-      uint32_t ab[KT][4];  // alpha as the B operand of dbasis (tokens x bases)
+      uint32_t ab[DB ? KT : 1][4];  // alpha as the B operand of dbasis (tokens x bases)
+      if constexpr (DB) {
 #pragma unroll
-      for (int kt = 0; kt < KT; ++kt) ldsm_x4_t(a_s + (16 * b) * L::ARB + kt * 32 + a_lane, ab[kt]);
+        for (int kt = 0; kt < KT; ++kt) ldsm_x4_t(a_s + (16 * b) * L::ARB + kt * 32 + a_lane, ab[kt]);
+      }
       uint32_t dyu[4];  // dy of this block, packed bf16 pairs (no activation)
       float dzu[2][4];  // fp32 dz of this block (SiLU)
       if constexpr (ACT) {
@@ -566,23 +582,27 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
             m[r] = hmul2_bf16(dyu[r], xr[r]);
           }
         }
+        if constexpr (DXDA) {
 #pragma unroll
-        for (int kt = 0; kt < KT; ++kt) {
-          if constexpr (BREG) {
-            mma_bf16(daa[2 * kt], m, bd[s][kt][0], bd[s][kt][1]);
-            mma_bf16(daa[2 * kt + 1], m, bd[s][kt][2], bd[s][kt][3]);
-          } else {
-            uint32_t bb[4];
-            ldsm_x4(basis_base + (s * KP + kt * 16) * kRowB + bn_lane, bb);
-            mma_bf16(daa[2 * kt], m, bb[0], bb[1]);
-            mma_bf16(daa[2 * kt + 1], m, bb[2], bb[3]);
+          for (int kt = 0; kt < KT; ++kt) {
+            if constexpr (BREG) {
+              mma_bf16(daa[2 * kt], m, bd[s][kt][0], bd[s][kt][1]);
+              mma_bf16(daa[2 * kt + 1], m, bd[s][kt][2], bd[s][kt][3]);
+            } else {
+              uint32_t bb[4];
+              ldsm_x4(basis_base + (s * KP + kt * 16) * kRowB + bn_lane, bb);
+              mma_bf16(daa[2 * kt], m, bb[0], bb[1]);
+              mma_bf16(daa[2 * kt + 1], m, bb[2], bb[3]);
+            }
           }
         }
-        uint32_t mt[4] = {movm_t(m[0]), movm_t(m[2]), movm_t(m[1]), movm_t(m[3])};
+        if constexpr (DB) {
+          uint32_t mt[4] = {movm_t(m[0]), movm_t(m[2]), movm_t(m[1]), movm_t(m[3])};
 #pragma unroll
-        for (int kt = 0; kt < KT; ++kt) {
-          mma_bf16(dba[s][2 * kt], mt, ab[kt][0], ab[kt][1]);
-          mma_bf16(dba[s][2 * kt + 1], mt, ab[kt][2], ab[kt][3]);
+          for (int kt = 0; kt < KT; ++kt) {
+            mma_bf16(dba[s][2 * kt], mt, ab[kt][0], ab[kt][1]);
+            mma_bf16(dba[s][2 * kt + 1], mt, ab[kt][2], ab[kt][3]);
+          }
         }
       }
       if (want_dx) {
@@ -600,6 +620,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
       }
       // dalpha partial of this warp's 16 channels -> red_s[b % RB][warp]; the CTA adds the
       // 8 warps once every RB blocks (and after the tile's last block)
+      if constexpr (!DXDA) continue;
       float* red = red_s + ((b % L::RB) * 8 + warp) * 16 * KP;
 #pragma unroll
       for (int kn = 0; kn < 2 * KT; ++kn)
@@ -628,9 +649,10 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true>::min_block
   }
 
   // dbasis partial of this CTA: db_part[group][k][s][ch]
+  if constexpr (!DB) return;
   const int64_t grp = blockIdx.y;
 #pragma unroll
-  for (int s = 0; s < S; ++s)
+  for (int s = 0; s < (DB ? S : 1); ++s)
 #pragma unroll
     for (int kn = 0; kn < 2 * KT; ++kn)
 #pragma unroll
@@ -740,21 +762,42 @@ int fwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alph
 template <int KT, int S, bool ACT>
 int bwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alpha, const void* dy, void* dalpha,
              void* dbasis, cudaStream_t st) {
-  using L = Layout<KT, S, ACT, true>;
+  // the layout of the launch (of the first pass when split); both passes share one plan
+  using L = Layout<KT, S, ACT, true, bwd_split(KT, S) ? kBwdDxDa : kBwdAll>;
   static_assert(L::min_blocks == ((L::BREG && !ACT && KT == 1) ? 2 : 1), "bwd_min_blocks() mirrors Layout::min_blocks");
   const Plan pl = make_plan(p, L::min_blocks);
   args.rm = pl.rm;
   args.items_per_group = pl.ipg;
   const int64_t nk = p.n_tokens * p.n_bases;
   const int64_t ksd = static_cast<int64_t>(p.n_bases) * p.kernel_size * p.dim;
-  static bool configured[64] = {};
-  int rc = configure(reinterpret_cast<const void*>(k_tc_bwd<KT, S, ACT>), configured, L::total);
+  // the attribute calls come first: they also make the device's primary context current,
+  // which the tensor-map encoding (a driver call) needs
+  int rc = MOC_OK;
+  if constexpr (bwd_split(KT, S)) {
+    using LB = Layout<KT, S, ACT, true, kBwdDb>;
+    static_assert(LB::min_blocks == 1, "one plan for both passes");
+    static bool conf_a[64] = {}, conf_b[64] = {};
+    rc = configure(reinterpret_cast<const void*>(k_tc_bwd<KT, S, ACT, kBwdDxDa>), conf_a, L::total);
+    if (rc == MOC_OK) rc = configure(reinterpret_cast<const void*>(k_tc_bwd<KT, S, ACT, kBwdDb>), conf_b, LB::total);
+  } else {
+    static bool configured[64] = {};
+    rc = configure(reinterpret_cast<const void*>(k_tc_bwd<KT, S, ACT, kBwdAll>), configured, L::total);
+  }
   if (rc != MOC_OK) return rc;
   Maps m;
   rc = make_maps<L, true>(p, x, dy, alpha, m);
   if (rc != MOC_OK) return rc;
-  k_tc_bwd<KT, S, ACT><<<dim3(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups)), kThreads, L::total,
-                         st>>>(m.x, m.dy, m.a, args);
+  const dim3 grid(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups));
+  if constexpr (bwd_split(KT, S)) {
+    k_tc_bwd<KT, S, ACT, kBwdDxDa><<<grid, kThreads, L::total, st>>>(m.x, m.dy, m.a, args);
+    note_launch();
+    rc = note_cuda(cudaGetLastError());
+    if (rc != MOC_OK) return rc;
+    k_tc_bwd<KT, S, ACT, kBwdDb><<<grid, kThreads, Layout<KT, S, ACT, true, kBwdDb>::total, st>>>(m.x, m.dy, m.a,
+                                                                                                  args);
+  } else {
+    k_tc_bwd<KT, S, ACT, kBwdAll><<<grid, kThreads, L::total, st>>>(m.x, m.dy, m.a, args);
+  }
   note_launch();
   rc = note_cuda(cudaGetLastError());
   if (rc != MOC_OK) return rc;
@@ -776,6 +819,7 @@ int dispatch(const moc_problem& p, Args&&... args) {
   MOC_TC_CASE(1, 1) MOC_TC_CASE(1, 2) MOC_TC_CASE(1, 3) MOC_TC_CASE(1, 4)
   MOC_TC_CASE(1, 5) MOC_TC_CASE(1, 6) MOC_TC_CASE(1, 7) MOC_TC_CASE(1, 8)
   MOC_TC_CASE(2, 1) MOC_TC_CASE(2, 2) MOC_TC_CASE(2, 3) MOC_TC_CASE(2, 4)
+  MOC_TC_CASE(2, 5) MOC_TC_CASE(2, 6) MOC_TC_CASE(2, 7) MOC_TC_CASE(2, 8)
 #undef MOC_TC_CASE
   return MOC_ERR_UNSUPPORTED_SHAPE;
 }
@@ -818,7 +862,6 @@ bool tc_conv_supported(const moc_problem& p) {
   if (p.x_dtype != MOC_DTYPE_BF16 || p.alpha_dtype != MOC_DTYPE_BF16 || p.basis_dtype != MOC_DTYPE_BF16) return false;
   if (p.n_bases % 8 != 0 || p.n_bases > 32) return false;
   if (p.kernel_size < 1 || p.kernel_size > 8) return false;
-  if (p.n_bases > 16 && p.kernel_size > 4) return false;
   if (p.dim % 8 != 0) return false;
   if (p.cu_seqlens != nullptr && p.chunk_size != kTile) return false;
   if (ceil_div(p.dim, kBD) > 65535) return false;

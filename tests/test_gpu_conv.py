@@ -135,6 +135,33 @@ def test_backward_is_bitwise_deterministic():
         assert torch.equal(t1, t2)
 
 
+def test_first_call_on_a_fresh_thread():
+    """A thread whose first CUDA work is this library's call (as the autograd engine's
+    device thread can be) gets the same results as the thread that made the earlier calls."""
+    import threading
+
+    x, a, dy, basis = _inputs(2, 128, 256, 32, 8, seed=5)
+    args = [t.bfloat16().cuda() for t in (x, a, basis, dy, dy)]
+    ref = ops.launch_backward(*args, activation_flag=0, need_x=True)
+    torch.cuda.synchronize()
+    box = {}
+
+    def work():
+        try:
+            box["out"] = ops.launch_backward(*args, activation_flag=0, need_x=True)
+            torch.cuda.synchronize()
+        except Exception as e:  # re-raised on the test thread
+            box["err"] = e
+
+    t = threading.Thread(target=work)
+    t.start()
+    t.join()
+    if "err" in box:
+        raise box["err"]
+    for t1, t2 in zip(ref, box["out"]):
+        assert torch.equal(t1, t2)
+
+
 def test_need_x_false_skips_dx():
     x, a, dy, basis = _inputs(2, 64, 64, 8, 4)
     dx, da, db = ops.launch_backward(x.cuda(), a.cuda(), basis.cuda(), dy.cuda(), dy.cuda(),
@@ -275,6 +302,25 @@ def test_larger_shapes_bf16(kernel_path, B, T, D, K, S):
     x, a, dy, basis = _inputs(B, T, D, K, S, seed=7)
     got, ref = _run(x, a, basis, dy, torch.bfloat16, torch.bfloat16, torch.bfloat16, "silu")
     _assert_close(got, ref, torch.bfloat16, f"shape {(B, T, D, K, S)}")
+
+
+@pytest.mark.parametrize("K,S,act", [(32, 8, None), (32, 8, "silu"), (32, 5, "silu"), (24, 6, None),
+                                     (32, 7, None), (17, 8, "silu")])
+def test_many_bases_long_kernels(kernel_path, K, S, act):
+    """Up to 32 bases with up to 8 taps (the large data-parallel config is K=32, S=8): the
+    basis sits in shared memory and the forward / backward run one CTA per SM."""
+    x, a, dy, basis = _inputs(2, 160, 384, K, S, seed=11)
+    got, ref = _run(x, a, basis, dy, torch.bfloat16, torch.bfloat16, torch.bfloat16, act)
+    _assert_close(got, ref, torch.bfloat16, f"K={K} S={S} act={act}")
+
+
+def test_many_bases_long_kernels_varlen(kernel_path):
+    lengths = [5, 70, 1, 8, 130, 64]
+    cu = torch.tensor([0] + torch.tensor(lengths).cumsum(0).tolist(), dtype=torch.int32)
+    x, a, dy, basis = _inputs(1, int(cu[-1]), 256, 32, 8, seed=12)
+    got, ref = _run(x[0], a[0], basis, dy[0], torch.bfloat16, torch.bfloat16, torch.bfloat16, None, cu=cu,
+                    max_seqlen=max(lengths))
+    _assert_close(got, ref, torch.bfloat16, "varlen K=32 S=8")
 
 
 def test_generic_and_tensor_core_paths_agree():
