@@ -228,6 +228,34 @@ typedef struct moc_decode_module {
 int moc_decode_step_multi(int32_t n_modules, const moc_decode_module* modules, int64_t batch,
                           int64_t z_dim, const void* z, void* stream);
 
+/* Fused projection + convolution forward (bf16, fixed-length sequences):
+ *
+ *   out = MoC(h . weight^T)   h [batch * seq_len, in_dim], weight [dim, in_dim] (nn.Linear
+ *                             layout), alpha [batch * seq_len, n_bases], basis [n_bases,
+ *                             kernel_size, dim], out [batch * seq_len, dim]; all bf16,
+ *                             row-major, contiguous, 16-byte aligned.
+ *
+ * The projection feeding a MoC module (the q, k or v slice of the reference's qkv_proj,
+ * README.md:115-129) runs on the tensor cores (tcgen05, accumulators in tensor memory) with
+ * the convolution as its epilogue: the projected x is rounded to bf16 on chip, as the
+ * reference's bf16 qkv tensor is, and never written to memory.  Forward only (inference and
+ * prefill without a cache); training runs the projection and moc_forward / moc_backward
+ * separately.  Requires n_bases % 8 == 0 and n_bases <= 16, 1 <= kernel_size <= 8,
+ * in_dim % 8 == 0 and dim % 8 == 0.  Not in the reference, which applies MoC after a
+ * separate projection GEMM. */
+typedef struct moc_proj_problem {
+  int64_t batch, seq_len;
+  int64_t in_dim, dim;
+  int32_t n_bases, kernel_size, activation;
+  int32_t reserved;
+  const void* h;
+  const void* weight;
+  const void* alpha;
+  const void* basis;
+  void* out;
+} moc_proj_problem;
+int moc_proj_forward(const moc_proj_problem* problem, void* stream);
+
 /* Gradient all-reduce over NVLink peer memory, for the data-parallel step (one process
  * per GPU).  The step's only collective sums the parameter gradients (conv_bases and
  * router) over ranks; at 640 KiB it is latency-bound, and this replaces the NCCL

@@ -123,12 +123,13 @@ uint64_t moc_launch_count(void) { return g_launches.load(std::memory_order_relax
 
 int moc_device_status(int* status, int clear) {
   if (status == nullptr) return MOC_ERR_INVALID_ARGUMENT;
-  int r = 0, c = 0, m = 0;
+  int r = 0, c = 0, m = 0, j = 0;
   int rc = router_status(&r, clear != 0);
   if (rc == MOC_OK) rc = conv_status(&c, clear != 0);
   if (rc == MOC_OK) rc = comm_status(&m, clear != 0);
+  if (rc == MOC_OK) rc = proj_status(&j, clear != 0);
   if (rc != MOC_OK) return rc;
-  *status = r | c | m;
+  *status = r | c | m | j;
   return MOC_OK;
 }
 
@@ -214,6 +215,24 @@ int moc_decode_step_multi(int32_t n_modules, const moc_decode_module* modules, i
   if (!z) return MOC_ERR_INVALID_ARGUMENT;
   if (!a16(z)) return MOC_ERR_MISALIGNED;
   return decode_step_multi(n_modules, modules, batch, z_dim, z, static_cast<cudaStream_t>(stream));
+}
+
+int moc_proj_forward(const moc_proj_problem* p, void* stream) {
+  if (!p) return MOC_ERR_INVALID_ARGUMENT;
+  if (p->batch < 0 || p->seq_len < 0 || p->in_dim <= 0 || p->dim <= 0 || p->n_bases <= 0 || p->kernel_size <= 0)
+    return MOC_ERR_INVALID_ARGUMENT;
+  if (p->activation != 0 && p->activation != 1) return MOC_ERR_INVALID_ARGUMENT;
+  if (p->n_bases % 8 != 0 || p->n_bases > 16 || p->kernel_size > 8 || p->in_dim % 8 != 0 || p->dim % 8 != 0)
+    return MOC_ERR_UNSUPPORTED_SHAPE;
+  // tensor-map coordinates are 32-bit
+  const int64_t lim = (int64_t{1} << 31) - 1024;
+  if (p->seq_len > lim || (p->seq_len > 0 && p->batch > lim / p->seq_len) || p->in_dim > lim || p->dim > lim)
+    return MOC_ERR_UNSUPPORTED_SHAPE;
+  if (p->batch == 0 || p->seq_len == 0) return MOC_OK;
+  if (!p->h || !p->weight || !p->alpha || !p->basis || !p->out) return MOC_ERR_INVALID_ARGUMENT;
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  if (!a16(p->h) || !a16(p->weight) || !a16(p->alpha) || !a16(p->basis) || !a16(p->out)) return MOC_ERR_MISALIGNED;
+  return proj_forward(*p, static_cast<cudaStream_t>(stream));
 }
 
 int moc_comm_create(int32_t rank, int32_t world, int64_t capacity, moc_comm** comm, void* handle_out) {

@@ -53,6 +53,10 @@ int tc_router_backward_noalloc(int64_t N, int64_t Dz, int K, int act, const void
 // fused decode step of up to MOC_DECODE_MAX_MODULES modules sharing z (moc_decode.cu)
 int decode_step_multi(int n, const moc_decode_module* mods, int64_t B, int64_t Dz, const void* z, cudaStream_t st);
 
+// fused projection GEMM (tcgen05) + convolution forward (moc_proj.cu)
+int proj_forward(const moc_proj_problem& p, cudaStream_t st);
+int proj_status(int* out, bool clear);
+
 // gradient all-reduce over NVLink peer memory (moc_comm.cu); CommImpl is the object
 // behind the C ABI's opaque moc_comm
 struct CommImpl;

@@ -1,0 +1,491 @@
+// Fused projection + MoC convolution forward, bf16, on the sm_100a tensor cores (tcgen05).
+//
+//   y = MoC(h . Wp^T)      h [N, Dm], Wp [D, Dm] (nn.Linear layout), y [N, D]
+//
+// In the reference's attention block (README.md:115-129) each MoC module convolves one slice
+// of the qkv projection.  Here the projection runs as a tcgen05 GEMM and the convolution is
+// its epilogue, so the projected x never goes to HBM (the unfused path writes x and reads it
+// back: 4 bytes per element).  The projection is rounded to bf16 before the convolution, as
+// the reference's bf16 qkv tensor is.
+//
+// Work decomposition: a tile is 128 GEMM rows x 256 output channels.  Its first 8 rows are
+// the causal halo (the tokens before the tile's 120 output rows, recomputed rather than
+// exchanged), so a sequence of T tokens takes ceil(T / 120) tiles and tiles never span two
+// sequences.  One persistent CTA per SM; CTA c takes tiles c, c + grid, ... in an order with
+// the channel tile innermost, so the CTAs running together share a few h row tiles and all
+// of Wp stays in L2 (each h tile comes from HBM about once):
+//   warp 0     TMA producer: h and Wp k-blocks (64 columns, 128-byte swizzle) into a
+//              3-stage ring (48 KB a stage);
+//   warp 1     allocates all 512 TMEM columns (two 128 x 256 fp32 accumulators) and issues
+//              tcgen05.mma (M=128, N=256, K=16) from one thread, committing each stage back
+//              to the producer and each finished accumulator to the epilogue;
+//   warps 4-11 epilogue, in two 128-channel passes per tile: tcgen05.ld the accumulator
+//              (warp w reads TMEM lanes 32 (w % 4)..),
+//              round to bf16 into a swizzled x tile in shared memory (rows before the
+//              sequence start zeroed), release the accumulator, then convolve exactly as the
+//              standalone forward does (W_s = alpha . basis_s on mma.sync, FFMA2 taps, fused
+//              SiLU) and store y through per-warp staging rows with 16-byte stores.
+// The two accumulators let the MMAs of tile i+1 run under the epilogue of tile i.
+//
+// Every mbarrier wait is bounded.  A wait that runs out records MOC_STATUS_WAIT_TIMEOUT and
+// raises a CTA-wide abort flag; every role then leaves its loop, the producer waits (bounded)
+// for the copies it issued, the MMA thread for its MMAs, and the TMEM is freed before exit.
+// Epilogue decisions to leave are made together (a barrier reduction), so no warp is left
+// at a named barrier.
+#include <algorithm>
+
+#include "moc_common.cuh"
+#include "moc_internal.h"
+#include "moc_mma.cuh"
+#include "moc_tma.cuh"
+
+namespace moc {
+
+__device__ int g_proj_status;
+
+namespace {
+
+constexpr int kPM = 128;              // GEMM rows per tile
+constexpr int kPHalo = 8;             // of which halo rows (S - 1 <= 7)
+constexpr int kPOut = kPM - kPHalo;   // output rows per tile
+constexpr int kPN = 256;              // output channels per tile (the MMA's N)
+constexpr int kPC = 128;              // channels per epilogue pass (two passes per tile)
+constexpr int kPK = 64;               // k per stage: 128-byte rows
+constexpr int kPStages = 3;
+constexpr int kPThreads = 384;        // 12 warps
+constexpr int kPEpiWarp0 = 4;         // epilogue warps 4..11
+constexpr int kPEpiThreads = 256;
+constexpr int kPATile = kPM * kPK * 2;         // 16 KB: h rows of one stage
+constexpr int kPStageBytes = kPATile + kPN * kPK * 2;  // + 32 KB of Wp rows
+constexpr int kPXR = kPM + 16;        // staged x rows: the last 16-row block reads up to 8 past the tile
+constexpr int kPXBox = kPXR * 128;    // one 64-channel half of the x tile
+constexpr int kPRowB = (kPC + 8) * 2; // basis row in shared memory (padded: conflict-free ldmatrix)
+constexpr int kPKP = 16;              // bases padded to the MMA K
+constexpr int kPARB = kPKP * 2;       // alpha row bytes
+constexpr int kPTmemCols = 2 * kPN;   // two accumulators
+constexpr uint32_t kPollAbortEvery = 1024;
+
+template <int S>
+struct ProjLayout {
+  static constexpr int x_off = kPStages * kPStageBytes;
+  static constexpr int a_off = x_off + 2 * kPXBox;
+  static constexpr int b_off = a_off + kPM * kPARB;
+  static constexpr int o_off = b_off + S * kPKP * kPRowB;
+  static constexpr int bar_off = o_off + 8 * 512;
+  static constexpr int n_bars = 2 * kPStages + 4 + 1;  // full, empty, acc full x2, acc empty x2, drain
+  static constexpr int misc_off = bar_off + 8 * n_bars;  // tmem slot, abort flag
+  static constexpr int total = 1024 + misc_off + 16;
+};
+
+struct ProjArgs {
+  const bf16* alpha;
+  const bf16* basis;
+  bf16* y;
+  int64_t seq_len, n_tokens;
+  int64_t dm, dout;
+  int K, act;
+  int64_t m_per_seq, m_tiles, n_tiles;
+};
+
+// ---- tcgen05 / barrier wrappers
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(slot), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[smem] . B[smem]^T, both K-major bf16, fp32 accumulate; one thread issues
+__device__ __forceinline__ void umma_bf16(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// arrives (once) on the mbarrier when every MMA this thread issued so far has completed
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+               : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
+// shared-memory matrix descriptor: K-major tile of 128-byte rows written by TMA with the
+// 128-byte swizzle (8-row groups 1024 bytes apart); sm_100 descriptor version 1
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+// instruction descriptor: bf16 A and B (K-major), fp32 D, M = 128, N = 256
+constexpr uint32_t kProjIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kPN >> 3) << 17) |
+                                (static_cast<uint32_t>(kPM >> 4) << 24);
+
+// named barrier over the epilogue warps; the second form also returns whether any of them
+// passed `p`
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(kPEpiThreads) : "memory"); }
+__device__ __forceinline__ bool epi_any(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred q, o;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred o, 1, %2, q;\n selp.u32 %0, 1, 0, o;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(p)), "n"(kPEpiThreads)
+      : "memory");
+  return r != 0;
+}
+
+// bounded wait that also gives up once another role raised the abort flag
+__device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, const volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kSpinLimit; i += kPollAbortEvery) {
+    if (mbar_wait(bar, parity, kPollAbortEvery)) return true;
+    if (*abort_flag) return false;
+  }
+  return false;
+}
+__device__ __forceinline__ void raise_abort(volatile int* abort_flag) {
+  *abort_flag = 1;
+  atomicOr(&g_proj_status, kStatusWaitTimeout);
+}
+
+struct TileCoord {
+  int64_t n0, m0, row0;  // first output channel, first output token, first GEMM row (m0 - halo)
+  int rows;              // output rows of this tile
+  bool seq_first;        // the halo rows precede the sequence start
+};
+
+__device__ __forceinline__ TileCoord tile_coord(const ProjArgs& a, int64_t t) {
+  TileCoord c;
+  const int64_t m = t / a.n_tiles, n = t - m * a.n_tiles;
+  const int64_t seq = m / a.m_per_seq, ci = m - seq * a.m_per_seq;
+  c.n0 = n * kPN;
+  c.m0 = seq * a.seq_len + ci * kPOut;
+  c.row0 = c.m0 - kPHalo;
+  c.rows = static_cast<int>(std::min<int64_t>(kPOut, a.seq_len - ci * kPOut));
+  c.seq_first = ci == 0;
+  return c;
+}
+
+template <int S, bool ACT>
+__global__ void __launch_bounds__(kPThreads, 1)
+    k_proj_conv(const __grid_constant__ CUtensorMap hmap, const __grid_constant__ CUtensorMap wmap, ProjArgs a) {
+  using L = ProjLayout<S>;
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_addr(base);
+  char* x_s = base + L::x_off;
+  char* a_s = base + L::a_off;
+  char* b_s = base + L::b_off;
+  char* o_s = base + L::o_off;
+  const uint32_t bar_full = sbase + L::bar_off;
+  const uint32_t bar_empty = bar_full + 8 * kPStages;
+  const uint32_t bar_accf = bar_empty + 8 * kPStages;
+  const uint32_t bar_acce = bar_accf + 16;
+  const uint32_t bar_drain = bar_acce + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + L::misc_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(base + L::misc_off + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t total_tiles = a.m_tiles * a.n_tiles;
+  const int64_t t_begin = blockIdx.x, t_step = gridDim.x;
+  const int nk = static_cast<int>((a.dm + kPK - 1) / kPK);
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&hmap);
+    tma_prefetch_desc(&wmap);
+    for (int i = 0; i < L::n_bars; ++i) mbar_init(bar_full + 8 * i, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(smem_addr(tmem_slot), kPTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int64_t issued = 0;
+      bool ok = true;
+      for (int64_t t = t_begin; t < total_tiles && ok; t += t_step) {
+        const TileCoord c = tile_coord(a, t);
+        for (int kb = 0; kb < nk; ++kb, ++issued) {
+          const int s = static_cast<int>(issued % kPStages);
+          const uint32_t use = static_cast<uint32_t>(issued / kPStages);
+          if (use > 0 && !wait_or_abort(bar_empty + 8 * s, (use & 1) ^ 1, abort_flag)) {
+            raise_abort(abort_flag);
+            ok = false;
+            break;
+          }
+          const uint32_t dst = sbase + s * kPStageBytes;
+          mbar_expect_tx(bar_full + 8 * s, kPStageBytes);
+          tma_load_2d(dst, &hmap, kb * kPK, static_cast<int>(c.row0), bar_full + 8 * s);
+          tma_load_2d(dst + kPATile, &wmap, kb * kPK, static_cast<int>(c.n0), bar_full + 8 * s);
+        }
+      }
+      if (!ok) {  // the copies still in flight land before the CTA's shared memory is released
+        for (int64_t i = std::max<int64_t>(0, issued - kPStages); i < issued; ++i)
+          mbar_wait(bar_full + 8 * static_cast<int>(i % kPStages), static_cast<uint32_t>(i / kPStages) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int64_t consumed = 0;
+      bool ok = true;
+      int li = 0;
+      for (int64_t t = t_begin; t < total_tiles && ok; t += t_step, ++li) {
+        const int buf = li & 1;
+        const uint32_t ub = static_cast<uint32_t>(li >> 1);
+        if (ub > 0 && !wait_or_abort(bar_acce + 8 * buf, (ub & 1) ^ 1, abort_flag)) {
+          raise_abort(abort_flag);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * kPN);
+        for (int kb = 0; kb < nk; ++kb, ++consumed) {
+          const int s = static_cast<int>(consumed % kPStages);
+          if (!wait_or_abort(bar_full + 8 * s, static_cast<uint32_t>(consumed / kPStages) & 1, abort_flag)) {
+            raise_abort(abort_flag);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(sbase + s * kPStageBytes);
+          const uint64_t bd = sw128_desc(sbase + s * kPStageBytes + kPATile);
+#pragma unroll
+          for (int k = 0; k < kPK / 16; ++k)  // +32 bytes per K=16 step inside the swizzled rows
+            umma_bf16(d, ad + 2 * k, bd + 2 * k, kProjIdesc, (kb | k) != 0);
+          umma_commit(bar_empty + 8 * s);
+        }
+        if (ok) umma_commit(bar_accf + 8 * buf);
+      }
+      // every MMA issued has completed before the TMEM is released
+      umma_commit(bar_drain);
+      mbar_wait(bar_drain, 0);
+    }
+    __syncwarp();
+  } else if (warp >= kPEpiWarp0) {
+    // ---------------------------------------------------------------- epilogue
+    const int e = warp - kPEpiWarp0;        // 16-channel group of the convolution
+    const int et = threadIdx.x - kPEpiWarp0 * 32;
+    const int quarter = warp & 3;  // a warp reads TMEM lanes 32 (warp id % 4) .. + 31
+    const int half = e >> 2;       // and accumulator columns 64 half .. + 63
+    const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8;
+    const int lcol = (lane >> 4) * 8;
+    const uint32_t xs = smem_addr(x_s);
+    const uint32_t x_box = static_cast<uint32_t>((e >> 2) * kPXBox);
+    const int x_chunk = 2 * (e & 3) + (lane >> 4);
+    const uint32_t a_lane = static_cast<uint32_t>(lrow * kPARB + lcol * 2);
+    const uint32_t ost_w = smem_addr(o_s + e * 512);
+    uint32_t bw[S][4];  // basis fragments of this warp's 16 channels
+    int li = 0;
+    for (int64_t t = t_begin; t < total_tiles; t += t_step, ++li) {
+      const TileCoord c = tile_coord(a, t);
+      const int buf = li & 1;
+      const uint32_t ub = static_cast<uint32_t>(li >> 1);
+      // the tile's channels in 128-channel halves (the second only where it has channels)
+      const int halves = c.n0 + kPC < a.dout ? 2 : 1;
+      // alpha rows of the tile's output tokens
+      {
+        const int r = et >> 1, chunk = et & 1;
+        const bool ok = r < c.rows && chunk * 8 < a.K;
+        const bf16* src = ok ? a.alpha + (c.m0 + r) * a.K + chunk * 8 : a.alpha;
+        cp_async16(smem_addr(a_s + r * kPARB + chunk * 16), src, ok ? 16u : 0u);
+      }
+      bool ok = true;
+      for (int hh = 0; hh < halves; ++hh) {
+        const int64_t c0 = c.n0 + hh * kPC;  // first channel of this half
+        // the basis slice of the half's channels
+        for (int idx = et; idx < S * kPKP * 16; idx += kPEpiThreads) {
+          const int row = idx >> 4, chunk = idx & 15;
+          const int s = row / kPKP, k = row - s * kPKP;
+          const int64_t ch = c0 + chunk * 8;
+          const bool in = k < a.K && ch < a.dout;
+          const bf16* src = in ? a.basis + (static_cast<int64_t>(k) * S + s) * a.dout + ch : a.basis;
+          cp_async16(smem_addr(b_s + row * kPRowB + chunk * 16), src, in ? 16u : 0u);
+        }
+        cp_async_commit();
+        if (hh == 0) {  // the accumulator of this tile
+          const bool landed = wait_or_abort(bar_accf + 8 * buf, ub & 1, abort_flag);
+          if (epi_any(!landed)) {
+            if (et == 0) raise_abort(abort_flag);
+            cp_async_wait<0>();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        {
+          // TMEM lane 32 quarter + lane = GEMM row r; 64 columns of it -> bf16 x row r
+          const int r = 32 * quarter + lane;
+          const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) +
+                                 static_cast<uint32_t>(buf * kPN + hh * kPC + 64 * half);
+          uint32_t v0[32], v1[32];
+          tmem_ld32(taddr, v0);
+          tmem_ld32(taddr + 32, v1);
+          tmem_ld_wait();
+          const bool zero = c.seq_first && r < kPHalo;  // tokens of the previous sequence
+          char* row_p = x_s + half * kPXBox + r * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t* v = j < 4 ? v0 + 8 * j : v1 + 8 * (j - 4);
+            uint4 w;
+            w.x = zero ? 0u : pack_bf16(__uint_as_float(v[0]), __uint_as_float(v[1]));
+            w.y = zero ? 0u : pack_bf16(__uint_as_float(v[2]), __uint_as_float(v[3]));
+            w.z = zero ? 0u : pack_bf16(__uint_as_float(v[4]), __uint_as_float(v[5]));
+            w.w = zero ? 0u : pack_bf16(__uint_as_float(v[6]), __uint_as_float(v[7]));
+            *reinterpret_cast<uint4*>(row_p + ((j ^ (r & 7)) << 4)) = w;
+          }
+        }
+        if (hh == halves - 1) tc_fence_before();
+        cp_async_wait<0>();
+        epi_sync();  // x tile, alpha and basis in shared memory
+        if (hh == halves - 1 && et == 0) mbar_arrive(bar_acce + 8 * buf);  // every warp is done with the accumulator
+#pragma unroll
+        for (int s = 0; s < S; ++s)
+          ldsm_x4_t(smem_addr(b_s + (s * kPKP + lrow) * kPRowB + (e * 16 + lcol) * 2), bw[s]);
+        // ---- the convolution of the tile's output rows (x row = output row + halo)
+        const int64_t ch_w = c0 + e * 16;
+        bf16* out_tile = a.y + c.m0 * a.dout + ch_w;
+        const int nb = (c.rows + 15) >> 4;
+        const uint32_t as = smem_addr(a_s);
+#pragma unroll 1
+        for (int b = 0; b < nb; ++b) {
+          uint32_t af[4];
+          ldsm_x4(as + (16 * b) * kPARB + a_lane, af);
+          float acc[2][4] = {};
+#pragma unroll
+          for (int s = 0; s < S; ++s) {
+            const int j = S - 1 - s;
+            float w[2][4];
+            mma_bf16_z(w[0], af, bw[s][0], bw[s][1]);
+            mma_bf16_z(w[1], af, bw[s][2], bw[s][3]);
+            uint32_t xr[4];
+            const int xrow = kPHalo + 16 * b - j + lrow;
+            ldsm_x4(xs + x_box + xrow * 128 + (((x_chunk ^ xrow) & 7) << 4), xr);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+              ffma2(acc[nt][0], acc[nt][1], w[nt][0], w[nt][1], bf_lo(xr[2 * nt]), bf_hi(xr[2 * nt]));
+              ffma2(acc[nt][2], acc[nt][3], w[nt][2], w[nt][3], bf_lo(xr[2 * nt + 1]), bf_hi(xr[2 * nt + 1]));
+            }
+          }
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int nt = i >> 1, h = i & 1;
+            float v0 = acc[nt][2 * h], v1 = acc[nt][2 * h + 1];
+            if (ACT) {
+              v0 = silu_bf(v0);
+              v1 = silu_bf(v1);
+            }
+            o[i] = pack_bf16(v0, v1);
+          }
+          __syncwarp();
+          stsm_x4(ost_w + lrow * 32 + ((((lane >> 4) ^ (lrow >> 2)) & 1) << 4), o[0], o[1], o[2], o[3]);
+          __syncwarp();
+          const int row = lane >> 1, hc = lane & 1;
+          const uint4 v = *reinterpret_cast<const uint4*>(o_s + e * 512 + row * 32 + ((hc ^ (row >> 2)) & 1) * 16);
+          if (16 * b + row < c.rows && ch_w + hc * 8 < a.dout)
+            *reinterpret_cast<uint4*>(out_tile + (16 * b + row) * a.dout + hc * 8) = v;
+        }
+        epi_sync();  // the x tile, alpha and basis are rewritten next
+      }
+      if (!ok) break;
+    }
+  }
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kPTmemCols);
+}
+
+template <int S, bool ACT>
+int proj_inst(const moc_proj_problem& p, ProjArgs& args, cudaStream_t st) {
+  using L = ProjLayout<S>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return note_cuda(e);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(k_proj_conv<S, ACT>),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
+    if (e != cudaSuccess) return note_cuda(e);
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  CUtensorMap hmap, wmap;
+  int rc = make_tmap_bf16_2d(&hmap, p.h, static_cast<uint64_t>(p.in_dim), static_cast<uint64_t>(args.n_tokens),
+                             static_cast<uint64_t>(p.in_dim) * 2, kPK, kPM, true);
+  if (rc == MOC_OK)
+    rc = make_tmap_bf16_2d(&wmap, p.weight, static_cast<uint64_t>(p.in_dim), static_cast<uint64_t>(p.dim),
+                           static_cast<uint64_t>(p.in_dim) * 2, kPK, kPN, true);
+  if (rc != MOC_OK) return rc;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t grid = std::min<int64_t>(std::max(sms, 1), args.m_tiles * args.n_tiles);
+  k_proj_conv<S, ACT><<<static_cast<unsigned>(grid), kPThreads, L::total, st>>>(hmap, wmap, args);
+  note_launch();
+  return note_cuda(cudaGetLastError());
+}
+
+}  // namespace
+
+int proj_forward(const moc_proj_problem& p, cudaStream_t st) {
+  ProjArgs a{};
+  a.alpha = static_cast<const bf16*>(p.alpha);
+  a.basis = static_cast<const bf16*>(p.basis);
+  a.y = static_cast<bf16*>(p.out);
+  a.seq_len = p.seq_len;
+  a.n_tokens = p.batch * p.seq_len;
+  a.dm = p.in_dim;
+  a.dout = p.dim;
+  a.K = p.n_bases;
+  a.act = p.activation;
+  a.m_per_seq = ceil_div(p.seq_len, kPOut);
+  a.m_tiles = p.batch * a.m_per_seq;
+  a.n_tiles = ceil_div(p.dim, kPN);
+  if (a.n_tokens == 0 || p.dim == 0) return MOC_OK;
+  const bool act = p.activation != 0;
+#define MOC_PROJ_CASE(s) \
+  if (p.kernel_size == s) return act ? proj_inst<s, true>(p, a, st) : proj_inst<s, false>(p, a, st);
+  MOC_PROJ_CASE(1) MOC_PROJ_CASE(2) MOC_PROJ_CASE(3) MOC_PROJ_CASE(4)
+  MOC_PROJ_CASE(5) MOC_PROJ_CASE(6) MOC_PROJ_CASE(7) MOC_PROJ_CASE(8)
+#undef MOC_PROJ_CASE
+  return MOC_ERR_UNSUPPORTED_SHAPE;
+}
+
+int proj_status(int* out, bool clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_proj_status, sizeof(int));
+  if (e != cudaSuccess) return note_cuda(e);
+  if (clear && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_proj_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return note_cuda(e);
+  }
+  *out = v;
+  return MOC_OK;
+}
+
+}  // namespace moc

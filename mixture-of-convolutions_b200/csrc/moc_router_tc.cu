@@ -185,7 +185,8 @@ struct BwdLayout {
   static constexpr int z_bytes = 2 * zbox;       // 128 columns
   static constexpr int w_bytes = KP * kRowB;
   static constexpr int dl_bytes = kBwdTile * DLB;  // one of two dl buffers
-  static constexpr int total = 1024 + 2 * z_bytes + w_bytes + 2 * dl_bytes + 64;
+  static constexpr int ost_bytes = 8 * 16 * 32;   // per-warp dz staging: 16 rows x 16 columns bf16
+  static constexpr int total = 1024 + 2 * z_bytes + w_bytes + 2 * dl_bytes + ost_bytes + 64;
 };
 
 struct RouterBwdArgs {
@@ -198,6 +199,8 @@ struct RouterBwdArgs {
   int64_t N, Dz;
   int K, act;
   int64_t tiles_per_group;
+  int vec_ad;  // alpha and dalpha bf16 and 16-byte aligned: vector loads of a thread's bases
+  int vec_dz;  // dz 16-byte aligned: 16-byte stores of staged rows
 };
 
 // TMA-staged backward: thread 0 double-buffers 64-token x 128-column z tiles (two
@@ -212,7 +215,8 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
   const uint32_t z_st = smem_addr(smem);
   char* w_s = smem + 2 * L::z_bytes;
   char* dl_s = w_s + L::w_bytes;
-  const uint32_t bar0 = smem_addr(dl_s + 2 * L::dl_bytes);
+  char* ost = dl_s + 2 * L::dl_bytes;
+  const uint32_t bar0 = smem_addr(ost + L::ost_bytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int64_t col_base = static_cast<int64_t>(blockIdx.x) * kZC;
@@ -267,6 +271,31 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
   float av[KQ], dv[KQ];
   auto fetch = [&](int64_t tile) {
     const int64_t tok = tile * kBwdTile + dl_row;
+    if (a.vec_ad) {  // K % 8 == 0: a thread's KQ bases are all valid or all padding
+      uint32_t wa[KQ / 2] = {}, wd[KQ / 2] = {};
+      if (tok < a.N && dl_part * KQ < a.K) {
+        const bf16* pa = a.alpha + tok * a.K + dl_part * KQ;
+        const bf16* pd = static_cast<const bf16*>(a.dalpha) + tok * a.K + dl_part * KQ;
+        if constexpr (KQ == 4) {
+          const uint2 va = __ldg(reinterpret_cast<const uint2*>(pa)), vd = __ldg(reinterpret_cast<const uint2*>(pd));
+          wa[0] = va.x, wa[1] = va.y, wd[0] = vd.x, wd[1] = vd.y;
+        } else {
+#pragma unroll
+          for (int v = 0; v < KQ / 8; ++v) {
+            const uint4 va = __ldg(reinterpret_cast<const uint4*>(pa) + v);
+            const uint4 vd = __ldg(reinterpret_cast<const uint4*>(pd) + v);
+            wa[4 * v] = va.x, wa[4 * v + 1] = va.y, wa[4 * v + 2] = va.z, wa[4 * v + 3] = va.w;
+            wd[4 * v] = vd.x, wd[4 * v + 1] = vd.y, wd[4 * v + 2] = vd.z, wd[4 * v + 3] = vd.w;
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < KQ / 2; ++e) {
+        av[2 * e] = bf_lo(wa[e]), av[2 * e + 1] = bf_hi(wa[e]);
+        dv[2 * e] = bf_lo(wd[e]), dv[2 * e + 1] = bf_hi(wd[e]);
+      }
+      return;
+    }
 #pragma unroll
     for (int e = 0; e < KQ; ++e) {
       const int k = dl_part * KQ + e;
@@ -290,9 +319,17 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
       dot += __shfl_xor_sync(0xffffffffu, dot, 1);
       dot += __shfl_xor_sync(0xffffffffu, dot, 2);
       if (a.act != 0) dot = 0.f;
-      bf16* dst = reinterpret_cast<bf16*>(dl_cur + dl_row * L::DLB) + dl_part * KQ;
+      uint32_t o[KQ / 2];
 #pragma unroll
-      for (int e = 0; e < KQ; ++e) dst[e] = __float2bfloat16_rn(av[e] * (dv[e] - dot));
+      for (int e = 0; e < KQ / 2; ++e) o[e] = pack_bf16(av[2 * e] * (dv[2 * e] - dot), av[2 * e + 1] * (dv[2 * e + 1] - dot));
+      char* dst = dl_cur + dl_row * L::DLB + dl_part * KQ * 2;  // 8-byte (KQ 4) / 16-byte (KQ 8) aligned
+      if constexpr (KQ == 4) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(o[0], o[1]);
+      } else {
+#pragma unroll
+        for (int v = 0; v < KQ / 8; ++v)
+          *reinterpret_cast<uint4*>(dst + 16 * v) = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+      }
     }
     if (it + 1 < i1) fetch(it + 1);
     const bool landed = mbar_wait(bar0 + 8 * cur, parity);
@@ -323,15 +360,30 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
           mma_bf16(acc[0], af[kt], wb[kt][0], wb[kt][1]);
           mma_bf16(acc[1], af[kt], wb[kt][2], wb[kt][3]);
         }
-        bf16* dz_row = a.dz + (tok0 + 16 * b + g) * a.Dz + col_base + cw + 2 * q;
+        if (a.vec_dz) {
+          // the block's 16 x 16 dz go through the warp's staging rows (stmatrix) and leave
+          // as one 16-byte store per lane (a full 32-byte row segment per lane pair)
+          const int lr = lm_row(lane);
+          const uint32_t ost_w = smem_addr(ost + warp * 512);
+          __syncwarp();  // the previous block's staging rows have been read
+          stsm_x4(ost_w + lr * 32 + ((((lane >> 4) ^ (lr >> 2)) & 1) << 4), pack_bf16(acc[0][0], acc[0][1]),
+                  pack_bf16(acc[0][2], acc[0][3]), pack_bf16(acc[1][0], acc[1][1]), pack_bf16(acc[1][2], acc[1][3]));
+          __syncwarp();
+          const int row = lane >> 1, half = lane & 1;
+          const uint4 v = *reinterpret_cast<const uint4*>(ost + warp * 512 + row * 32 + ((half ^ (row >> 2)) & 1) * 16);
+          if (tok0 + 16 * b + row < a.N && col_base + cw + half * 8 < a.Dz)
+            *reinterpret_cast<uint4*>(a.dz + (tok0 + 16 * b + row) * a.Dz + col_base + cw + half * 8) = v;
+        } else {
+          bf16* dz_row = a.dz + (tok0 + 16 * b + g) * a.Dz + col_base + cw + 2 * q;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (tok0 + 16 * b + g + 8 * h < a.N) {
+          for (int h = 0; h < 2; ++h) {
+            if (tok0 + 16 * b + g + 8 * h < a.N) {
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-              if (col_base + cw + nt * 8 < a.Dz)
-                *reinterpret_cast<uint32_t*>(dz_row + 8 * h * a.Dz + nt * 8) =
-                    pack_bf16(acc[nt][2 * h], acc[nt][2 * h + 1]);
+              for (int nt = 0; nt < 2; ++nt)
+                if (col_base + cw + nt * 8 < a.Dz)
+                  *reinterpret_cast<uint32_t*>(dz_row + 8 * h * a.Dz + nt * 8) =
+                      pack_bf16(acc[nt][2 * h], acc[nt][2 * h + 1]);
+            }
           }
         }
       }
@@ -476,6 +528,8 @@ int tc_router_backward(int64_t N, int64_t Dz, int K, int act, const void* z, con
   a.Dz = Dz;
   a.K = K;
   a.act = act;
+  a.vec_ad = da_dtype == MOC_DTYPE_BF16 && aligned16(alpha) && aligned16(dalpha) && K % 8 == 0;
+  a.vec_dz = dz != nullptr && aligned16(dz);
   int64_t slices, groups, tpg;
   bwd_plan(N, Dz, slices, groups, tpg);
   a.tiles_per_group = tpg;

@@ -1,4 +1,5 @@
-"""Fused decode step for MoC modules that share their routing input.
+"""Fused paths around MoC modules: the decode step of modules that share their routing
+input, and the projection that feeds a module with the convolution as its epilogue.
 
 In the reference's attention block (README.md:120-129) the q, k and v short convolutions
 are three MoC modules routed by the same ``x_norm``.  Decoding one token through them one
@@ -110,3 +111,46 @@ def decode_step(modules: Sequence[MoC], xs: Sequence[torch.Tensor], z: torch.Ten
                                                _lib.stream_of(z2.device))
     _lib.check(rc, "moc_decode_step_multi")
     return [y.reshape(xo.shape) for y, xo in zip(ys, xs)]
+
+
+def proj_forward(h: torch.Tensor, weight: torch.Tensor, module: MoC, z: torch.Tensor | None = None,
+                 alpha: torch.Tensor | None = None) -> torch.Tensor:
+    """``module(h @ weight.T, z)[0]`` in one kernel: the projection runs on the tensor cores and
+    the convolution is its epilogue, so the projected tensor never reaches memory.
+
+    h:      [B, T, in_dim] bf16, fixed-length sequences (no cache, no packing).
+    weight: [module.dim, in_dim] bf16, the module's slice of the projection (nn.Linear layout:
+            for the reference's attention block, the q, k or v rows of qkv_proj.weight).
+    z:      the routing input [B, T, z_dim]; or ``alpha`` [B, T, module.k], the router output.
+
+    Forward only (no autograd graph): inference and prefill.  The projection is rounded to
+    bf16 before the convolution, as a bf16 qkv tensor is; the result matches the unfused
+    path up to the order of the projection's fp32 sums."""
+    if h.ndim != 3 or h.dtype != torch.bfloat16 or not h.is_cuda:
+        raise ValueError(f"h must be a CUDA bf16 tensor [B, T, in_dim], got {tuple(h.shape)} {h.dtype}")
+    B, T, Dm = h.shape
+    if weight.shape != (module.dim, Dm) or weight.dtype != torch.bfloat16:
+        raise ValueError(f"weight must be bf16 [{module.dim}, {Dm}], got {tuple(weight.shape)} {weight.dtype}")
+    if module.conv_bases.dtype != torch.bfloat16:
+        raise ValueError("proj_forward needs a bf16 module")
+    if (alpha is None) == (z is None):
+        raise ValueError("pass exactly one of z (routing input) or alpha (router output)")
+    from . import ops
+
+    if alpha is None:
+        if z.shape[:2] != (B, T):
+            raise ValueError(f"z must be [{B}, {T}, z_dim], got {tuple(z.shape)}")
+        alpha = ops.launch_router_forward(z.detach(), module.router.detach(), module.router_activation)
+    if alpha.shape != (B, T, module.k) or alpha.dtype != torch.bfloat16:
+        raise ValueError(f"alpha must be bf16 [{B}, {T}, {module.k}], got {tuple(alpha.shape)} {alpha.dtype}")
+    h2, w2, a2 = _aligned(h.detach()), _aligned(weight.detach()), _aligned(alpha.detach())
+    basis = _aligned(module.conv_bases.detach())
+    out = torch.empty(B, T, module.dim, dtype=torch.bfloat16, device=h.device)
+    prob = _lib.MocProjProblem(batch=B, seq_len=T, in_dim=Dm, dim=module.dim, n_bases=module.k,
+                               kernel_size=module.kernel_size, activation=int(module.activation is not None),
+                               h=h2.data_ptr(), weight=w2.data_ptr(), alpha=a2.data_ptr(),
+                               basis=basis.data_ptr(), out=out.data_ptr())
+    with torch.cuda.device(h.device):
+        rc = _lib.load().moc_proj_forward(ctypes.byref(prob), _lib.stream_of(h.device))
+    _lib.check(rc, "moc_proj_forward")
+    return out

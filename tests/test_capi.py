@@ -126,7 +126,8 @@ def _c_layout(struct: str, fields: list[str]) -> dict[str, int]:
 
 
 @pytest.mark.parametrize("struct,mirror", [("moc_problem", _lib.MocProblem),
-                                           ("moc_decode_module", _lib.MocDecodeModule)])
+                                           ("moc_decode_module", _lib.MocDecodeModule),
+                                           ("moc_proj_problem", _lib.MocProjProblem)])
 def test_ctypes_structs_match_the_header_layout(struct, mirror):
     names = [f[0] for f in mirror._fields_]
     layout = _c_layout(struct, names)
@@ -161,6 +162,29 @@ def test_decode_multi_checks():
     two[1].kernel_size = 2
     assert lib.moc_decode_step_multi(2, two, 4, 64, 2048, None) == 3  # one kernel size for all modules
     assert lib.moc_decode_step_multi(2, mods(2), 0, 64, 2048, None) == 0  # empty batch: no work
+
+
+def test_proj_checks():
+    lib = _lib.load()
+
+    def prob(**kw):
+        f = dict(batch=2, seq_len=64, in_dim=256, dim=128, n_bases=16, kernel_size=4, activation=0, h=256,
+                 weight=512, alpha=768, basis=1024, out=1280)
+        f.update(kw)
+        return ctypes.byref(_lib.MocProjProblem(**f))
+
+    assert lib.moc_proj_forward(None, None) == 1
+    assert lib.moc_proj_forward(prob(n_bases=32), None) == 3    # at most 16 bases
+    assert lib.moc_proj_forward(prob(n_bases=12), None) == 3    # n_bases % 8
+    assert lib.moc_proj_forward(prob(kernel_size=9), None) == 3
+    assert lib.moc_proj_forward(prob(in_dim=100), None) == 3    # in_dim % 8
+    assert lib.moc_proj_forward(prob(dim=132), None) == 3       # dim % 8
+    assert lib.moc_proj_forward(prob(dim=0), None) == 1
+    assert lib.moc_proj_forward(prob(activation=2), None) == 1
+    assert lib.moc_proj_forward(prob(seq_len=1 << 40), None) == 3  # 32-bit tensor-map coordinates
+    assert lib.moc_proj_forward(prob(weight=0), None) == 1
+    assert lib.moc_proj_forward(prob(out=1288), None) == 4      # 16-byte alignment
+    assert lib.moc_proj_forward(prob(batch=0), None) == 0       # no tokens: no work
 
 
 def test_comm_checks():

@@ -112,6 +112,36 @@ def test_router_forward_backward(dtype, K, router_act):
     assert rel_err(dw, wr.grad) <= TOL[dtype]
 
 
+@pytest.mark.parametrize("K", [16, 32])
+@pytest.mark.parametrize("router_act", ["softmax", "exp"])
+def test_router_backward_scalar_and_vector_paths_agree(K, router_act):
+    """bf16 alpha / dalpha are fetched with vector loads and dz leaves through 16-byte
+    stores when aligned; fp32 dalpha and a dz that is only 4-byte aligned take the
+    per-element paths.  Same arithmetic, so the results are bitwise equal."""
+    g = torch.Generator().manual_seed(15)
+    N, Dz = 2 * 97, 320
+    kz = torch.randn(N, Dz, generator=g).bfloat16().cuda()
+    kw = (torch.randn(K, Dz, generator=g) * 0.05).bfloat16().cuda()
+    da = torch.randn(N, K, generator=g).bfloat16().cuda()
+    alpha = ops.launch_router_forward(kz, kw, router_act)
+    dz_ref, dw_ref = ops.launch_router_backward(kz, kw, alpha, da, router_act)
+    dz32, dw32 = ops.launch_router_backward(kz, kw, alpha, da.float(), router_act)
+    assert torch.equal(dz32, dz_ref) and torch.equal(dw32, dw_ref)
+
+    lib = _lib.load()
+    buf = torch.empty(N * Dz + 2, dtype=torch.bfloat16, device="cuda")
+    dz = buf[2:].view(N, Dz)  # 4-byte, not 16-byte, aligned
+    dw = torch.empty_like(kw)
+    code = _lib.dtype_code(kz)
+    ws_bytes = lib.moc_router_backward_workspace_bytes(N, Dz, K, code)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    rc = lib.moc_router_backward(N, Dz, K, code, ops.ROUTER_ACTIVATIONS[router_act], _lib.ptr(kz), _lib.ptr(kw),
+                                 _lib.ptr(alpha), _lib.ptr(da), code, _lib.ptr(dz), _lib.ptr(dw), _lib.ptr(ws),
+                                 ws_bytes, _lib.stream_of(kz.device))
+    _lib.check(rc, "moc_router_backward")
+    assert torch.equal(dz, dz_ref) and torch.equal(dw, dw_ref)
+
+
 # ------------------------------------------------------------------ decode
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "fp32"])
