@@ -8,28 +8,33 @@
 // back: 4 bytes per element).  The projection is rounded to bf16 before the convolution, as
 // the reference's bf16 qkv tensor is.
 //
-// Work decomposition: a tile is 128 GEMM rows x 256 output channels.  Its first 8 rows are
-// the causal halo (the tokens before the tile's 120 output rows, recomputed rather than
-// exchanged), so a sequence of T tokens takes ceil(T / 120) tiles and tiles never span two
-// sequences.  One persistent CTA per SM; CTA c takes tiles c, c + grid, ... in an order with
-// the channel tile innermost, so the CTAs running together share a few h row tiles and all
-// of Wp stays in L2 (each h tile comes from HBM about once):
-//   warp 0     TMA producer: h and Wp k-blocks (64 columns, 128-byte swizzle) into a
-//              3-stage ring (48 KB a stage);
-//   warp 1     allocates all 512 TMEM columns (two 128 x 256 fp32 accumulators) and issues
-//              tcgen05.mma (M=128, N=256, K=16) from one thread, committing each stage back
-//              to the producer and each finished accumulator to the epilogue;
+// Work decomposition: an m-tile is 128 GEMM rows whose first 8 are the causal halo (the
+// tokens before its 120 output rows, recomputed rather than exchanged), so a sequence of T
+// tokens takes ceil(T / 120) m-tiles and m-tiles never span two sequences.  The two CTAs of
+// a cluster (two SMs) share one tcgen05.mma of M = 256 (each CTA's 128 rows) by N = 256
+// output channels: each stages its own h rows and half of the Wp rows (32 KB a stage), so a
+// staged byte feeds twice the MMA work of a one-SM 128 x 128 tile.  One persistent cluster
+// per SM pair takes tile pairs c, c + clusters, ... with the channel tile innermost, so the
+// clusters running together share a few h row tiles and all of Wp stays in L2:
+//   warp 0     TMA producer (both CTAs): h and Wp k-blocks (64 columns, 128-byte swizzle)
+//              into a 4-stage ring, completing on the leader CTA's stage barrier;
+//   warp 1     allocates all 512 TMEM columns in both CTAs (two 128 x 256 fp32 accumulators
+//              each); in the leader CTA one thread issues tcgen05.mma.cta_group::2 (M=256,
+//              N=256, K=16), committing each stage back to both producers and each finished
+//              accumulator to both epilogues (multicast commit; no load uses multicast);
 //   warps 4-11 epilogue, in two 128-channel passes per tile: tcgen05.ld the accumulator
 //              (warp w reads TMEM lanes 32 (w % 4)..),
 //              round to bf16 into a swizzled x tile in shared memory (rows before the
 //              sequence start zeroed), release the accumulator, then convolve exactly as the
 //              standalone forward does (W_s = alpha . basis_s on mma.sync, FFMA2 taps, fused
 //              SiLU) and store y through per-warp staging rows with 16-byte stores.
-// The two accumulators let the MMAs of tile i+1 run under the epilogue of tile i.
+// The two accumulators let the MMAs of tile i+1 run under the epilogue of tile i; the
+// leader reuses an accumulator once both CTAs' epilogues have released it.
 //
 // Every mbarrier wait is bounded.  A wait that runs out records MOC_STATUS_WAIT_TIMEOUT and
-// raises a CTA-wide abort flag; every role then leaves its loop, the producer waits (bounded)
-// for the copies it issued, the MMA thread for its MMAs, and the TMEM is freed before exit.
+// raises a CTA-wide abort flag; every role then leaves its loop, the producers wait (bounded)
+// for the copies they issued, the MMA thread for its MMAs, and both CTAs meet at a cluster
+// barrier before the TMEM is freed.
 // Epilogue decisions to leave are made together (a barrier reduction), so no warp is left
 // at a named barrier.
 #include <algorithm>
@@ -49,14 +54,15 @@ constexpr int kPM = 128;              // GEMM rows per tile
 constexpr int kPHalo = 8;             // of which halo rows (S - 1 <= 7)
 constexpr int kPOut = kPM - kPHalo;   // output rows per tile
 constexpr int kPN = 256;              // output channels per tile (the MMA's N)
+constexpr int kPNH = kPN / 2;         // Wp rows staged by each CTA of the pair
 constexpr int kPC = 128;              // channels per epilogue pass (two passes per tile)
 constexpr int kPK = 64;               // k per stage: 128-byte rows
-constexpr int kPStages = 3;
+constexpr int kPStages = 4;
 constexpr int kPThreads = 384;        // 12 warps
 constexpr int kPEpiWarp0 = 4;         // epilogue warps 4..11
 constexpr int kPEpiThreads = 256;
 constexpr int kPATile = kPM * kPK * 2;         // 16 KB: h rows of one stage
-constexpr int kPStageBytes = kPATile + kPN * kPK * 2;  // + 32 KB of Wp rows
+constexpr int kPStageBytes = kPATile + kPNH * kPK * 2;  // + 16 KB of Wp rows
 constexpr int kPXR = kPM + 16;        // staged x rows: the last 16-row block reads up to 8 past the tile
 constexpr int kPXBox = kPXR * 128;    // one 64-channel half of the x tile
 constexpr int kPRowB = (kPC + 8) * 2; // basis row in shared memory (padded: conflict-free ldmatrix)
@@ -85,6 +91,7 @@ struct ProjArgs {
   int64_t dm, dout;
   int K, act;
   int64_t m_per_seq, m_tiles, n_tiles;
+  int64_t pair_tiles;  // ceil(m_tiles / 2) x n_tiles
 };
 
 // ---- tcgen05 / barrier wrappers
@@ -92,27 +99,68 @@ struct ProjArgs {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 
+// executed by the same warp of both CTAs of the pair
 __device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(slot), "r"(ncols)
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(slot), "r"(ncols)
                : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::: "memory");
 }
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
-// D[tmem] (+)= A[smem] . B[smem]^T, both K-major bf16, fp32 accumulate; one thread issues
-__device__ __forceinline__ void umma_bf16(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+// D[tmem] (+)= A[smem] . B[smem]^T over the CTA pair (A: each CTA's 128 rows, B: each CTA's
+// half of the N rows; D: each CTA's TMEM), both K-major bf16, fp32 accumulate; one thread
+// of the leader CTA issues
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
 }
-// arrives (once) on the mbarrier when every MMA this thread issued so far has completed
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
-               : "memory");
+// arrives (once) on the mbarrier at this offset in both CTAs of the pair when every MMA this
+// thread issued so far has completed
+__device__ __forceinline__ void umma_commit_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n" ::"r"(
+          bar),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+// ... on the leader's own mbarrier only
+__device__ __forceinline__ void umma_commit_self(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(cluster_addr) : "memory");
+}
+// TMA tile load into this CTA's shared memory that completes on a barrier of either CTA of
+// the pair (the leader's: the MMA issuer waits for both CTAs' operands there)
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                                 uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(cluster_bar)
+      : "memory");
 }
 
 // 32 consecutive fp32 columns of this thread's TMEM lane
@@ -136,9 +184,9 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
          (static_cast<uint64_t>(2) << 61);
 }
-// instruction descriptor: bf16 A and B (K-major), fp32 D, M = 128, N = 256
+// instruction descriptor: bf16 A and B (K-major), fp32 D, M = 256 (the pair), N = 256
 constexpr uint32_t kProjIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kPN >> 3) << 17) |
-                                (static_cast<uint32_t>(kPM >> 4) << 24);
+                                (static_cast<uint32_t>((2 * kPM) >> 4) << 24);
 
 // named barrier over the epilogue warps; the second form also returns whether any of them
 // passed `p`
@@ -172,11 +220,21 @@ struct TileCoord {
   bool seq_first;        // the halo rows precede the sequence start
 };
 
-__device__ __forceinline__ TileCoord tile_coord(const ProjArgs& a, int64_t t) {
+// tile pair tp, CTA `rank` of the pair: m-tile 2 (tp / n_tiles) + rank, channel tile
+// tp % n_tiles.  A CTA past the last m-tile stages zero rows (coordinates past the end) and
+// stores nothing.
+__device__ __forceinline__ TileCoord tile_coord(const ProjArgs& a, int64_t tp, uint32_t rank) {
   TileCoord c;
-  const int64_t m = t / a.n_tiles, n = t - m * a.n_tiles;
-  const int64_t seq = m / a.m_per_seq, ci = m - seq * a.m_per_seq;
+  const int64_t pm = tp / a.n_tiles, n = tp - pm * a.n_tiles;
+  const int64_t m = 2 * pm + rank;
   c.n0 = n * kPN;
+  if (m >= a.m_tiles) {
+    c.m0 = c.row0 = a.n_tokens;
+    c.rows = 0;
+    c.seq_first = false;
+    return c;
+  }
+  const int64_t seq = m / a.m_per_seq, ci = m - seq * a.m_per_seq;
   c.m0 = seq * a.seq_len + ci * kPOut;
   c.row0 = c.m0 - kPHalo;
   c.rows = static_cast<int>(std::min<int64_t>(kPOut, a.seq_len - ci * kPOut));
@@ -185,7 +243,7 @@ __device__ __forceinline__ TileCoord tile_coord(const ProjArgs& a, int64_t t) {
 }
 
 template <int S, bool ACT>
-__global__ void __launch_bounds__(kPThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     k_proj_conv(const __grid_constant__ CUtensorMap hmap, const __grid_constant__ CUtensorMap wmap, ProjArgs a) {
   using L = ProjLayout<S>;
   extern __shared__ __align__(1024) char smem_raw[];
@@ -204,20 +262,25 @@ __global__ void __launch_bounds__(kPThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + L::misc_off + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t total_tiles = a.m_tiles * a.n_tiles;
-  const int64_t t_begin = blockIdx.x, t_step = gridDim.x;
+  const uint32_t rank = cluster_rank();
+  const int64_t total_tiles = a.pair_tiles;
+  const int64_t t_begin = blockIdx.x >> 1, t_step = gridDim.x >> 1;
   const int nk = static_cast<int>((a.dm + kPK - 1) / kPK);
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&hmap);
     tma_prefetch_desc(&wmap);
-    for (int i = 0; i < L::n_bars; ++i) mbar_init(bar_full + 8 * i, 1);
+    // the accumulator-empty pair is released by both CTAs' epilogues (the leader's is used)
+    for (int i = 0; i < L::n_bars; ++i) {
+      const uint32_t bar = bar_full + 8 * i;
+      mbar_init(bar, bar == bar_acce || bar == bar_acce + 8 ? 2 : 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(smem_addr(tmem_slot), kPTmemCols);
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -226,8 +289,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
     if (lane == 0) {
       int64_t issued = 0;
       bool ok = true;
+      const uint32_t leader_full = peer_addr(bar_full, 0);
       for (int64_t t = t_begin; t < total_tiles && ok; t += t_step) {
-        const TileCoord c = tile_coord(a, t);
+        const TileCoord c = tile_coord(a, t, rank);
         for (int kb = 0; kb < nk; ++kb, ++issued) {
           const int s = static_cast<int>(issued % kPStages);
           const uint32_t use = static_cast<uint32_t>(issued / kPStages);
@@ -237,20 +301,24 @@ __global__ void __launch_bounds__(kPThreads, 1)
             break;
           }
           const uint32_t dst = sbase + s * kPStageBytes;
-          mbar_expect_tx(bar_full + 8 * s, kPStageBytes);
-          tma_load_2d(dst, &hmap, kb * kPK, static_cast<int>(c.row0), bar_full + 8 * s);
-          tma_load_2d(dst + kPATile, &wmap, kb * kPK, static_cast<int>(c.n0), bar_full + 8 * s);
+          if (rank == 0) mbar_expect_tx(bar_full + 8 * s, 2 * kPStageBytes);  // both CTAs' bytes
+          tma_load_2d_pair(dst, &hmap, kb * kPK, static_cast<int>(c.row0), leader_full + 8 * s);
+          tma_load_2d_pair(dst + kPATile, &wmap, kb * kPK, static_cast<int>(c.n0 + rank * kPNH), leader_full + 8 * s);
         }
       }
       if (!ok) {  // the copies still in flight land before the CTA's shared memory is released
-        for (int64_t i = std::max<int64_t>(0, issued - kPStages); i < issued; ++i)
-          mbar_wait(bar_full + 8 * static_cast<int>(i % kPStages), static_cast<uint32_t>(i / kPStages) & 1);
+        if (rank == 0) {
+          for (int64_t i = std::max<int64_t>(0, issued - kPStages); i < issued; ++i)
+            mbar_wait(bar_full + 8 * static_cast<int>(i % kPStages), static_cast<uint32_t>(i / kPStages) & 1);
+        } else {  // they complete on the leader's barriers: allow them a bounded time
+          for (int i = 0; i < 4096; ++i) __nanosleep(1000);
+        }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       int64_t consumed = 0;
       bool ok = true;
       int li = 0;
@@ -275,13 +343,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
           const uint64_t bd = sw128_desc(sbase + s * kPStageBytes + kPATile);
 #pragma unroll
           for (int k = 0; k < kPK / 16; ++k)  // +32 bytes per K=16 step inside the swizzled rows
-            umma_bf16(d, ad + 2 * k, bd + 2 * k, kProjIdesc, (kb | k) != 0);
-          umma_commit(bar_empty + 8 * s);
+            umma_bf16_pair(d, ad + 2 * k, bd + 2 * k, kProjIdesc, (kb | k) != 0);
+          umma_commit_both(bar_empty + 8 * s);
         }
-        if (ok) umma_commit(bar_accf + 8 * buf);
+        if (ok) umma_commit_both(bar_accf + 8 * buf);
       }
       // every MMA issued has completed before the TMEM is released
-      umma_commit(bar_drain);
+      umma_commit_self(bar_drain);
       mbar_wait(bar_drain, 0);
     }
     __syncwarp();
@@ -300,8 +368,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const uint32_t ost_w = smem_addr(o_s + e * 512);
     uint32_t bw[S][4];  // basis fragments of this warp's 16 channels
     int li = 0;
+    const uint32_t acce_leader = peer_addr(bar_acce, 0);
     for (int64_t t = t_begin; t < total_tiles; t += t_step, ++li) {
-      const TileCoord c = tile_coord(a, t);
+      const TileCoord c = tile_coord(a, t, rank);
       const int buf = li & 1;
       const uint32_t ub = static_cast<uint32_t>(li >> 1);
       // the tile's channels in 128-channel halves (the second only where it has channels)
@@ -361,7 +430,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (hh == halves - 1) tc_fence_before();
         cp_async_wait<0>();
         epi_sync();  // x tile, alpha and basis in shared memory
-        if (hh == halves - 1 && et == 0) mbar_arrive(bar_acce + 8 * buf);  // every warp is done with the accumulator
+        if (hh == halves - 1 && et == 0) mbar_arrive_cluster(acce_leader + 8 * buf);  // this CTA is done with it
 #pragma unroll
         for (int s = 0; s < S; ++s)
           ldsm_x4_t(smem_addr(b_s + (s * kPKP + lrow) * kPRowB + (e * 16 + lcol) * 2), bw[s]);
@@ -416,7 +485,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   }
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // the leader's MMAs into this CTA's TMEM and shared memory are done
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, kPTmemCols);
 }
@@ -439,12 +508,12 @@ int proj_inst(const moc_proj_problem& p, ProjArgs& args, cudaStream_t st) {
                              static_cast<uint64_t>(p.in_dim) * 2, kPK, kPM, true);
   if (rc == MOC_OK)
     rc = make_tmap_bf16_2d(&wmap, p.weight, static_cast<uint64_t>(p.in_dim), static_cast<uint64_t>(p.dim),
-                           static_cast<uint64_t>(p.in_dim) * 2, kPK, kPN, true);
+                           static_cast<uint64_t>(p.in_dim) * 2, kPK, kPNH, true);
   if (rc != MOC_OK) return rc;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t grid = std::min<int64_t>(std::max(sms, 1), args.m_tiles * args.n_tiles);
-  k_proj_conv<S, ACT><<<static_cast<unsigned>(grid), kPThreads, L::total, st>>>(hmap, wmap, args);
+  const int64_t clusters = std::min<int64_t>(std::max(sms / 2, 1), args.pair_tiles);
+  k_proj_conv<S, ACT><<<static_cast<unsigned>(2 * clusters), kPThreads, L::total, st>>>(hmap, wmap, args);
   note_launch();
   return note_cuda(cudaGetLastError());
 }
@@ -465,6 +534,7 @@ int proj_forward(const moc_proj_problem& p, cudaStream_t st) {
   a.m_per_seq = ceil_div(p.seq_len, kPOut);
   a.m_tiles = p.batch * a.m_per_seq;
   a.n_tiles = ceil_div(p.dim, kPN);
+  a.pair_tiles = ceil_div(a.m_tiles, int64_t{2}) * a.n_tiles;
   if (a.n_tokens == 0 || p.dim == 0) return MOC_OK;
   const bool act = p.activation != 0;
 #define MOC_PROJ_CASE(s) \
