@@ -49,6 +49,7 @@ CONFIG_LARGE = {"B": 4, "T": 8192, "D": 4096, "Dz": 4096, "K": 32, "S": 8, "rout
                 "init_std": (32 / (3 * 8)) ** 0.5, "router_std": 0.02}
 METRIC = "MoC fwd+bwd tokens/s"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 
 
 def step_bytes_per_token(D: int, Dz: int, K: int) -> int:
@@ -72,7 +73,10 @@ def measured_peaks() -> dict:
     if os.path.exists(path):
         with open(path) as f:
             d = json.load(f)
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+        out = {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+        if "bf16_tflops" in d:
+            out["bf16_tflops"] = float(d["bf16_tflops"])
+        return out
     return {"hbm_gbs": FALLBACK_HBM_GBS, "source": "fallback"}
 
 
@@ -470,6 +474,110 @@ def run_varlen(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
+PROJ = {"B": 4, "T": 4096, "d_model": 4096, "K": 16, "S": 4,
+        "modules": (("q", 4096, "exp"), ("k", 1024, "exp"), ("v", 1024, "softmax"))}
+
+
+def run_proj(args, rank: int, world: int, local_rank: int) -> None:
+    """The fused projection + convolution forward: the q / k / v MoC modules of an attention
+    block (README.md:115-129) at config 4's widths, prefill of B=4 x T=4096 tokens.  One step
+    is, per module, its router and one moc_proj_forward over its rows of qkv_proj.weight,
+    captured in a CUDA graph; beside it the unfused path (one cuBLAS qkv GEMM, then each
+    module's MoC forward on its slice).  Each rank runs its own batch (replicas)."""
+    from moc import MoC, _lib, fused
+    import moc.ops as ops
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
+    c = PROJ
+    B, T, Dm = c["B"], c["T"], c["d_model"]
+    torch.manual_seed(1234)
+    mods = []
+    for name, D, ract in c["modules"]:
+        m = MoC(dim=D, z_dim=Dm, kernel_size=c["S"], k=c["K"], init_std=0.002, router_activation=ract)
+        with torch.no_grad():
+            m.router.normal_(0.0, 0.02)
+        mods.append(m.to(device=device, dtype=torch.bfloat16))
+    g = torch.Generator().manual_seed(77 + rank)
+    d_total = sum(D for _, D, _ in c["modules"])
+    w_qkv = (torch.randn(d_total, Dm, generator=g) / Dm ** 0.5).bfloat16().to(device)
+    h = torch.randn(B, T, Dm, generator=g).bfloat16().to(device)  # x_norm: projected and routing input
+    offs = [0]
+    for _, D, _ in c["modules"]:
+        offs.append(offs[-1] + D)
+    w_rows = [w_qkv[offs[i]:offs[i + 1]] for i in range(len(mods))]
+
+    def step_fused():
+        return [fused.proj_forward(h, w, m, z=h) for m, w in zip(mods, w_rows)]
+
+    def step_unfused():
+        with torch.no_grad():
+            qkv = torch.matmul(h, w_qkv.T)
+            return [m(qkv[..., offs[i]:offs[i + 1]], h)[0] for i, m in enumerate(mods)]
+
+    # parity of the two paths on this workload (bf16 tolerance of the convolution tests)
+    for a_, b_ in zip(step_fused(), step_unfused()):
+        err = float((a_.float() - b_.float()).abs().max() / b_.float().abs().max().clamp_min(1e-30))
+        assert err <= 2e-2, f"fused and unfused paths differ: {err:.3e}"
+    for _ in range(args.warmup):
+        step_fused()
+    torch.cuda.synchronize()
+    l0 = _lib.launch_count()
+    step_fused()
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - l0
+    stream = torch.cuda.current_stream(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step_fused()
+    for _ in range(args.warmup):
+        graph.replay()
+    sampler = ClockSampler(device, os.environ.get("TMPDIR", "/tmp"))
+    barrier(world)
+    t0 = time.time()
+    ms = time_region(graph.replay, args.steps, stream)
+    t1 = time.time()
+    barrier(world)
+    ms = max_over_ranks(ms, world)
+    clocks = sampler.summary(t0, t1)
+    ms_unfused = graph_time(step_unfused, max(3, min(args.steps, 10)), device)
+    # the fused kernel alone on the widest module (router output precomputed)
+    alpha_q = ops.launch_router_forward(h, mods[0].router.detach(), mods[0].router_activation)
+    k_ms = graph_time(lambda: fused.proj_forward(h, w_rows[0], mods[0], alpha=alpha_q),
+                      max(3, min(args.steps, 10)), device)
+    k_flops = 2.0 * B * T * Dm * mods[0].dim
+    peaks = measured_peaks()
+    peak_tf = peaks.get("bf16_tflops", FALLBACK_BF16_TFLOPS)
+    tokens = B * T
+    if rank == 0:
+        print(json.dumps({
+            "metric": "MoC q/k/v projection + convolution prefill tokens/s", "value": tokens * world / (ms * 1e-3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "fused projection (next-step item 2): q D=4096 / k D=1024 / v D=1024 MoC modules "
+                                   "over d_model=4096, B=4, T=4096, K=16, S=4, routers exp/exp/softmax",
+                       "parallelism": f"replicas{world}",
+                       "timing": "CUDA graph of one step (3 routers + 3 fused launches) replayed K times; CUDA events"},
+            "unfused_ms_per_step": ms_unfused,
+            "unfused": "cuBLAS qkv GEMM (torch.matmul) + each module's router and MoC forward on its slice",
+            "roofline": {"bound": "tensor", "kernel": "k_proj_conv (q module, D=4096)", "achieved": k_flops / (k_ms * 1e-3) / 1e12,
+                         "peak": peak_tf, "peak_source": "measured" if "bf16_tflops" in peaks else "fallback",
+                         "unit": "TFLOP/s", "frac": k_flops / (k_ms * 1e-3) / 1e12 / peak_tf,
+                         "launch_ms": k_ms, "algorithmic_flops_per_launch": k_flops,
+                         "note": "projection FLOPs only; the 8 recomputed halo rows per 120 output rows and the "
+                                 "per-sequence tile padding are extra work not counted"},
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks,
+        }), flush=True)
+    sampler.stop()
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def bench_config(cfg: dict, world: int) -> dict:
     """The workload description both arms print."""
     if cfg["D"] == CONFIG_LARGE["D"]:
@@ -513,10 +621,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("train", "decode", "varlen", "large"), default="train",
+    ap.add_argument("--workload", choices=("train", "decode", "varlen", "large", "proj"), default="train",
                     help="train: config 2 (the headline); decode: config 4, three modules, batch 128; "
                          "varlen: config 3, packed sequences, exp router, SiLU; large: config 5, "
-                         "4 sequences of 8192 tokens per GPU, D=4096, K=32, S=8")
+                         "4 sequences of 8192 tokens per GPU, D=4096, K=32, S=8; proj: the fused projection + "
+                         "convolution forward of q/k/v modules (prefill)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -532,6 +641,9 @@ def main() -> None:
         return
     if args.workload == "varlen":
         run_varlen(args, rank, world, local_rank)
+        return
+    if args.workload == "proj":
+        run_proj(args, rank, world, local_rank)
         return
 
     from moc import _lib, dp
