@@ -11,8 +11,9 @@
 //                 stores its tile into CTA 0's shared memory (distributed shared memory),
 //                 and CTA 0 adds the 8 tiles in rank order and applies softmax / exp per
 //                 token over 16 lanes (moc/api.py:383-388).
-//   k_dec_update  CTA = (128 channels of one module, 16 tokens).  The basis slice, alpha,
-//                 x and cache tiles arrive with 16-byte copies; per tap, one ldmatrix of
+//   k_dec_update  CTA = (128 channels of one module, 16 tokens), launched as a programmatic
+//                 dependent of the router: the basis slice, x and cache tiles arrive with
+//                 16-byte copies while the router still runs, alpha once it has finished; per tap, one ldmatrix of
 //                 the basis and two mma.sync per warp form W_s = alpha . basis_s for 16
 //                 tokens x 16 channels (bf16 products exact, fp32 sums: the rounding of the
 //                 reference's bf16 forward, moc/kernels.py:125-130; its decode kernel rounds
@@ -77,6 +78,15 @@ struct DecArgs {
 __device__ __forceinline__ int lm_row_d(int lane) { return (lane & 7) + ((lane >> 3) & 1) * 8; }
 __device__ __forceinline__ int lm_col_d(int lane) { return (lane >> 4) * 8; }
 
+// Programmatic dependent launch: the router lets the update grid start at once; the update
+// kernel stages everything that does not depend on the router (basis, x, cache) and then
+// waits for the router grid's completion (and its alpha) before reading alpha.  Without the
+// launch attribute both are no-ops and the kernels run one after the other.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
@@ -105,6 +115,7 @@ __global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(256)
   const uint32_t rank = cluster_rank();
   const int64_t tok0 = static_cast<int64_t>(blockIdx.x / kDecCluster) * kDecTok;
   const int n_chunks = static_cast<int>((a.Dz + kDecCols - 1) / kDecCols);
+  griddep_launch_dependents();
 
   auto load = [&](int c, int st) {
     char* base = smem + st * kDecStageBytes;
@@ -240,6 +251,7 @@ __global__ void __launch_bounds__(kUpdThreads) k_dec_update(const __grid_constan
                ok ? mod.cache + ((b0 + t) * mod.D + c0) * S + p * 8 : mod.cache, ok ? 16u : 0u);
   }
   cp_async_commit();
+  griddep_wait();  // alpha comes from the router grid
   for (int i = threadIdx.x; i < kUpdTok * kDecKP; i += kUpdThreads) {
     const int t = i / kDecKP, k = i - t * kDecKP;
     const bool ok = t < ntok && k < mod.K;
@@ -340,8 +352,18 @@ cudaError_t launch_update(dim3 grid, const DecArgs& a, cudaStream_t st, int dev)
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  k_dec_update<S><<<grid, kUpdThreads, UpdLayout<S>::total, st>>>(a);
-  return cudaSuccess;
+  // launched as a programmatic dependent of the router (its loads overlap the router)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kUpdThreads);
+  cfg.dynamicSmemBytes = UpdLayout<S>::total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_dec_update<S>, a);
 }
 
 }  // namespace
