@@ -481,7 +481,7 @@ PROJ = {"B": 4, "T": 4096, "d_model": 4096, "K": 16, "S": 4,
 def run_proj(args, rank: int, world: int, local_rank: int) -> None:
     """The fused projection + convolution forward: the q / k / v MoC modules of an attention
     block (README.md:115-129) at config 4's widths, prefill of B=4 x T=4096 tokens.  One step
-    is, per module, its router and one moc_proj_forward over its rows of qkv_proj.weight,
+    is the three routers and one moc_proj_forward_multi over qkv_proj.weight (h read once),
     captured in a CUDA graph; beside it the unfused path (one cuBLAS qkv GEMM, then each
     module's MoC forward on its slice).  Each rank runs its own batch (replicas)."""
     from moc import MoC, _lib, fused
@@ -510,7 +510,7 @@ def run_proj(args, rank: int, world: int, local_rank: int) -> None:
     w_rows = [w_qkv[offs[i]:offs[i + 1]] for i in range(len(mods))]
 
     def step_fused():
-        return [fused.proj_forward(h, w, m, z=h) for m, w in zip(mods, w_rows)]
+        return fused.proj_forward_multi(h, w_qkv, mods, z=h)
 
     def step_unfused():
         with torch.no_grad():
@@ -559,7 +559,8 @@ def run_proj(args, rank: int, world: int, local_rank: int) -> None:
             "config": {"workload": "fused projection (next-step item 2): q D=4096 / k D=1024 / v D=1024 MoC modules "
                                    "over d_model=4096, B=4, T=4096, K=16, S=4, routers exp/exp/softmax",
                        "parallelism": f"replicas{world}",
-                       "timing": "CUDA graph of one step (3 routers + 3 fused launches) replayed K times; CUDA events"},
+                       "timing": "CUDA graph of one step (3 routers + 1 fused launch for q, k, v) replayed K times; "
+                                 "CUDA events"},
             "unfused_ms_per_step": ms_unfused,
             "unfused": "cuBLAS qkv GEMM (torch.matmul) + each module's router and MoC forward on its slice",
             "roofline": {"bound": "tensor", "kernel": "k_proj_conv (q module, D=4096)", "achieved": k_flops / (k_ms * 1e-3) / 1e12,

@@ -256,6 +256,25 @@ typedef struct moc_proj_problem {
 } moc_proj_problem;
 int moc_proj_forward(const moc_proj_problem* problem, void* stream);
 
+/* Several modules over one projection, in one launch: the reference's
+ *   q, k, v = qkv_proj(x_norm).split(...);  q = q_conv(q, x_norm); ...
+ * with weight = qkv_proj.weight [weight_rows, in_dim].  Module i takes weight rows
+ * [row_offset, row_offset + dim) and writes out [batch * seq_len, dim] from its alpha
+ * [batch * seq_len, n_bases] and basis [n_bases, kernel_size, dim].  h is read once for
+ * all modules.  Every module has the same kernel_size; the requirements of
+ * moc_proj_forward apply to each (n_bases % 8 == 0 and <= 16, dim % 8 == 0). */
+#define MOC_PROJ_MAX_MODULES 4
+typedef struct moc_proj_module {
+  int64_t dim, row_offset;
+  int32_t n_bases, activation;
+  const void* alpha;
+  const void* basis;
+  void* out;
+} moc_proj_module;
+int moc_proj_forward_multi(int32_t n_modules, const moc_proj_module* modules, int64_t batch, int64_t seq_len,
+                           int64_t in_dim, int32_t kernel_size, const void* h, const void* weight,
+                           int64_t weight_rows, void* stream);
+
 /* Gradient all-reduce over NVLink peer memory, for the data-parallel step (one process
  * per GPU).  The step's only collective sums the parameter gradients (conv_bases and
  * router) over ranks; at 640 KiB it is latency-bound, and this replaces the NCCL

@@ -217,22 +217,49 @@ int moc_decode_step_multi(int32_t n_modules, const moc_decode_module* modules, i
   return decode_step_multi(n_modules, modules, batch, z_dim, z, static_cast<cudaStream_t>(stream));
 }
 
-int moc_proj_forward(const moc_proj_problem* p, void* stream) {
-  if (!p) return MOC_ERR_INVALID_ARGUMENT;
-  if (p->batch < 0 || p->seq_len < 0 || p->in_dim <= 0 || p->dim <= 0 || p->n_bases <= 0 || p->kernel_size <= 0)
-    return MOC_ERR_INVALID_ARGUMENT;
-  if (p->activation != 0 && p->activation != 1) return MOC_ERR_INVALID_ARGUMENT;
-  if (p->n_bases % 8 != 0 || p->n_bases > 16 || p->kernel_size > 8 || p->in_dim % 8 != 0 || p->dim % 8 != 0)
-    return MOC_ERR_UNSUPPORTED_SHAPE;
+int moc_proj_forward_multi(int32_t n_modules, const moc_proj_module* modules, int64_t batch, int64_t seq_len,
+                           int64_t in_dim, int32_t kernel_size, const void* h, const void* weight,
+                           int64_t weight_rows, void* stream) {
+  if (n_modules < 1 || n_modules > MOC_PROJ_MAX_MODULES || !modules) return MOC_ERR_INVALID_ARGUMENT;
+  if (batch < 0 || seq_len < 0 || in_dim <= 0 || kernel_size <= 0 || weight_rows <= 0) return MOC_ERR_INVALID_ARGUMENT;
+  if (kernel_size > 8 || in_dim % 8 != 0) return MOC_ERR_UNSUPPORTED_SHAPE;
   // tensor-map coordinates are 32-bit
   const int64_t lim = (int64_t{1} << 31) - 1024;
-  if (p->seq_len > lim || (p->seq_len > 0 && p->batch > lim / p->seq_len) || p->in_dim > lim || p->dim > lim)
+  if (seq_len > lim || (seq_len > 0 && batch > lim / seq_len) || in_dim > lim || weight_rows > lim)
     return MOC_ERR_UNSUPPORTED_SHAPE;
-  if (p->batch == 0 || p->seq_len == 0) return MOC_OK;
-  if (!p->h || !p->weight || !p->alpha || !p->basis || !p->out) return MOC_ERR_INVALID_ARGUMENT;
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
-  if (!a16(p->h) || !a16(p->weight) || !a16(p->alpha) || !a16(p->basis) || !a16(p->out)) return MOC_ERR_MISALIGNED;
-  return proj_forward(*p, static_cast<cudaStream_t>(stream));
+  for (int i = 0; i < n_modules; ++i) {
+    const moc_proj_module& m = modules[i];
+    if (m.dim <= 0 || m.n_bases <= 0 || m.row_offset < 0) return MOC_ERR_INVALID_ARGUMENT;
+    if (m.activation != 0 && m.activation != 1) return MOC_ERR_INVALID_ARGUMENT;
+    if (m.row_offset > weight_rows - m.dim) return MOC_ERR_INVALID_ARGUMENT;  // rows past the weight
+    if (m.n_bases % 8 != 0 || m.n_bases > 16 || m.dim % 8 != 0) return MOC_ERR_UNSUPPORTED_SHAPE;
+    if (batch > 0 && seq_len > 0) {
+      if (!m.alpha || !m.basis || !m.out) return MOC_ERR_INVALID_ARGUMENT;
+      if (!a16(m.alpha) || !a16(m.basis) || !a16(m.out)) return MOC_ERR_MISALIGNED;
+    }
+  }
+  if (batch == 0 || seq_len == 0) return MOC_OK;
+  if (!h || !weight) return MOC_ERR_INVALID_ARGUMENT;
+  if (!a16(h) || !a16(weight)) return MOC_ERR_MISALIGNED;
+  return proj_forward_multi(n_modules, modules, batch, seq_len, in_dim, kernel_size, h, weight, weight_rows,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int moc_proj_forward(const moc_proj_problem* p, void* stream) {
+  if (!p) return MOC_ERR_INVALID_ARGUMENT;
+  if (p->dim <= 0) return MOC_ERR_INVALID_ARGUMENT;
+  if (p->dim % 8 != 0) return MOC_ERR_UNSUPPORTED_SHAPE;
+  moc_proj_module m{};
+  m.dim = p->dim;
+  m.row_offset = 0;
+  m.n_bases = p->n_bases;
+  m.activation = p->activation;
+  m.alpha = p->alpha;
+  m.basis = p->basis;
+  m.out = p->out;
+  return moc_proj_forward_multi(1, &m, p->batch, p->seq_len, p->in_dim, p->kernel_size, p->h, p->weight, p->dim,
+                                stream);
 }
 
 int moc_comm_create(int32_t rank, int32_t world, int64_t capacity, moc_comm** comm, void* handle_out) {

@@ -83,14 +83,23 @@ struct ProjLayout {
   static constexpr int total = 1024 + misc_off + 16;
 };
 
-struct ProjArgs {
+// one module: its rows of the weight, its router output, basis and output
+struct ProjMod {
   const bf16* alpha;
   const bf16* basis;
   bf16* y;
-  int64_t seq_len, n_tokens;
-  int64_t dm, dout;
+  int64_t dout;     // channels
+  int64_t row_off;  // first weight row
+  int64_t tile0;    // first channel tile (over all modules)
   int K, act;
-  int64_t m_per_seq, m_tiles, n_tiles;
+};
+
+struct ProjArgs {
+  ProjMod mod[MOC_PROJ_MAX_MODULES];
+  int n_mod;
+  int64_t seq_len, n_tokens, dm;
+  int64_t m_per_seq, m_tiles;
+  int64_t n_tiles;     // channel tiles over all modules
   int64_t pair_tiles;  // ceil(m_tiles / 2) x n_tiles
 };
 
@@ -215,19 +224,25 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag) {
 }
 
 struct TileCoord {
-  int64_t n0, m0, row0;  // first output channel, first output token, first GEMM row (m0 - halo)
+  int64_t n0, m0, row0;  // first output channel (of its module), first output token, first GEMM row (m0 - halo)
+  int64_t wrow0;         // first weight row
+  int mod;               // module
   int rows;              // output rows of this tile
   bool seq_first;        // the halo rows precede the sequence start
 };
 
 // tile pair tp, CTA `rank` of the pair: m-tile 2 (tp / n_tiles) + rank, channel tile
-// tp % n_tiles.  A CTA past the last m-tile stages zero rows (coordinates past the end) and
-// stores nothing.
+// tp % n_tiles (of the module whose tiles it falls in).  A CTA past the last m-tile stages
+// zero rows (coordinates past the end) and stores nothing.
 __device__ __forceinline__ TileCoord tile_coord(const ProjArgs& a, int64_t tp, uint32_t rank) {
   TileCoord c;
   const int64_t pm = tp / a.n_tiles, n = tp - pm * a.n_tiles;
   const int64_t m = 2 * pm + rank;
-  c.n0 = n * kPN;
+  int mi = 0;
+  while (mi + 1 < a.n_mod && n >= a.mod[mi + 1].tile0) ++mi;
+  c.mod = mi;
+  c.n0 = (n - a.mod[mi].tile0) * kPN;
+  c.wrow0 = a.mod[mi].row_off + c.n0;
   if (m >= a.m_tiles) {
     c.m0 = c.row0 = a.n_tokens;
     c.rows = 0;
@@ -242,7 +257,7 @@ __device__ __forceinline__ TileCoord tile_coord(const ProjArgs& a, int64_t tp, u
   return c;
 }
 
-template <int S, bool ACT>
+template <int S>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     k_proj_conv(const __grid_constant__ CUtensorMap hmap, const __grid_constant__ CUtensorMap wmap, ProjArgs a) {
   using L = ProjLayout<S>;
@@ -303,7 +318,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           const uint32_t dst = sbase + s * kPStageBytes;
           if (rank == 0) mbar_expect_tx(bar_full + 8 * s, 2 * kPStageBytes);  // both CTAs' bytes
           tma_load_2d_pair(dst, &hmap, kb * kPK, static_cast<int>(c.row0), leader_full + 8 * s);
-          tma_load_2d_pair(dst + kPATile, &wmap, kb * kPK, static_cast<int>(c.n0 + rank * kPNH), leader_full + 8 * s);
+          tma_load_2d_pair(dst + kPATile, &wmap, kb * kPK, static_cast<int>(c.wrow0 + rank * kPNH),
+                           leader_full + 8 * s);
         }
       }
       if (!ok) {  // the copies still in flight land before the CTA's shared memory is released
@@ -371,15 +387,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const uint32_t acce_leader = peer_addr(bar_acce, 0);
     for (int64_t t = t_begin; t < total_tiles; t += t_step, ++li) {
       const TileCoord c = tile_coord(a, t, rank);
+      const ProjMod& md = a.mod[c.mod];
       const int buf = li & 1;
       const uint32_t ub = static_cast<uint32_t>(li >> 1);
       // the tile's channels in 128-channel halves (the second only where it has channels)
-      const int halves = c.n0 + kPC < a.dout ? 2 : 1;
+      const int halves = c.n0 + kPC < md.dout ? 2 : 1;
       // alpha rows of the tile's output tokens
       {
         const int r = et >> 1, chunk = et & 1;
-        const bool ok = r < c.rows && chunk * 8 < a.K;
-        const bf16* src = ok ? a.alpha + (c.m0 + r) * a.K + chunk * 8 : a.alpha;
+        const bool ok = r < c.rows && chunk * 8 < md.K;
+        const bf16* src = ok ? md.alpha + (c.m0 + r) * md.K + chunk * 8 : md.alpha;
         cp_async16(smem_addr(a_s + r * kPARB + chunk * 16), src, ok ? 16u : 0u);
       }
       bool ok = true;
@@ -390,8 +407,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           const int row = idx >> 4, chunk = idx & 15;
           const int s = row / kPKP, k = row - s * kPKP;
           const int64_t ch = c0 + chunk * 8;
-          const bool in = k < a.K && ch < a.dout;
-          const bf16* src = in ? a.basis + (static_cast<int64_t>(k) * S + s) * a.dout + ch : a.basis;
+          const bool in = k < md.K && ch < md.dout;
+          const bf16* src = in ? md.basis + (static_cast<int64_t>(k) * S + s) * md.dout + ch : md.basis;
           cp_async16(smem_addr(b_s + row * kPRowB + chunk * 16), src, in ? 16u : 0u);
         }
         cp_async_commit();
@@ -436,7 +453,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           ldsm_x4_t(smem_addr(b_s + (s * kPKP + lrow) * kPRowB + (e * 16 + lcol) * 2), bw[s]);
         // ---- the convolution of the tile's output rows (x row = output row + halo)
         const int64_t ch_w = c0 + e * 16;
-        bf16* out_tile = a.y + c.m0 * a.dout + ch_w;
+        bf16* out_tile = md.y + c.m0 * md.dout + ch_w;
+        const bool act = md.act != 0;
         const int nb = (c.rows + 15) >> 4;
         const uint32_t as = smem_addr(a_s);
 #pragma unroll 1
@@ -464,7 +482,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           for (int i = 0; i < 4; ++i) {
             const int nt = i >> 1, h = i & 1;
             float v0 = acc[nt][2 * h], v1 = acc[nt][2 * h + 1];
-            if (ACT) {
+            if (act) {
               v0 = silu_bf(v0);
               v1 = silu_bf(v1);
             }
@@ -475,8 +493,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           __syncwarp();
           const int row = lane >> 1, hc = lane & 1;
           const uint4 v = *reinterpret_cast<const uint4*>(o_s + e * 512 + row * 32 + ((hc ^ (row >> 2)) & 1) * 16);
-          if (16 * b + row < c.rows && ch_w + hc * 8 < a.dout)
-            *reinterpret_cast<uint4*>(out_tile + (16 * b + row) * a.dout + hc * 8) = v;
+          if (16 * b + row < c.rows && ch_w + hc * 8 < md.dout)
+            *reinterpret_cast<uint4*>(out_tile + (16 * b + row) * md.dout + hc * 8) = v;
         }
         epi_sync();  // the x tile, alpha and basis are rewritten next
       }
@@ -490,59 +508,72 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kPTmemCols);
 }
 
-template <int S, bool ACT>
-int proj_inst(const moc_proj_problem& p, ProjArgs& args, cudaStream_t st) {
+template <int S>
+int proj_inst(ProjArgs& args, const void* h, const void* weight, int64_t weight_rows, cudaStream_t st) {
   using L = ProjLayout<S>;
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return note_cuda(e);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(k_proj_conv<S, ACT>),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(k_proj_conv<S>), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             L::total);
     if (e != cudaSuccess) return note_cuda(e);
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
   CUtensorMap hmap, wmap;
-  int rc = make_tmap_bf16_2d(&hmap, p.h, static_cast<uint64_t>(p.in_dim), static_cast<uint64_t>(args.n_tokens),
-                             static_cast<uint64_t>(p.in_dim) * 2, kPK, kPM, true);
+  int rc = make_tmap_bf16_2d(&hmap, h, static_cast<uint64_t>(args.dm), static_cast<uint64_t>(args.n_tokens),
+                             static_cast<uint64_t>(args.dm) * 2, kPK, kPM, true);
   if (rc == MOC_OK)
-    rc = make_tmap_bf16_2d(&wmap, p.weight, static_cast<uint64_t>(p.in_dim), static_cast<uint64_t>(p.dim),
-                           static_cast<uint64_t>(p.in_dim) * 2, kPK, kPNH, true);
+    rc = make_tmap_bf16_2d(&wmap, weight, static_cast<uint64_t>(args.dm), static_cast<uint64_t>(weight_rows),
+                           static_cast<uint64_t>(args.dm) * 2, kPK, kPNH, true);
   if (rc != MOC_OK) return rc;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t clusters = std::min<int64_t>(std::max(sms / 2, 1), args.pair_tiles);
-  k_proj_conv<S, ACT><<<static_cast<unsigned>(2 * clusters), kPThreads, L::total, st>>>(hmap, wmap, args);
+  k_proj_conv<S><<<static_cast<unsigned>(2 * clusters), kPThreads, L::total, st>>>(hmap, wmap, args);
   note_launch();
   return note_cuda(cudaGetLastError());
 }
 
 }  // namespace
 
-int proj_forward(const moc_proj_problem& p, cudaStream_t st) {
+int proj_forward_multi(int n, const moc_proj_module* mods, int64_t batch, int64_t seq_len, int64_t in_dim, int S,
+                       const void* h, const void* weight, int64_t weight_rows, cudaStream_t st) {
   ProjArgs a{};
-  a.alpha = static_cast<const bf16*>(p.alpha);
-  a.basis = static_cast<const bf16*>(p.basis);
-  a.y = static_cast<bf16*>(p.out);
-  a.seq_len = p.seq_len;
-  a.n_tokens = p.batch * p.seq_len;
-  a.dm = p.in_dim;
-  a.dout = p.dim;
-  a.K = p.n_bases;
-  a.act = p.activation;
-  a.m_per_seq = ceil_div(p.seq_len, kPOut);
-  a.m_tiles = p.batch * a.m_per_seq;
-  a.n_tiles = ceil_div(p.dim, kPN);
+  a.n_mod = n;
+  a.seq_len = seq_len;
+  a.n_tokens = batch * seq_len;
+  a.dm = in_dim;
+  a.m_per_seq = ceil_div(seq_len, kPOut);
+  a.m_tiles = batch * a.m_per_seq;
+  int64_t tiles = 0;
+  for (int i = 0; i < n; ++i) {
+    ProjMod& m = a.mod[i];
+    m.alpha = static_cast<const bf16*>(mods[i].alpha);
+    m.basis = static_cast<const bf16*>(mods[i].basis);
+    m.y = static_cast<bf16*>(mods[i].out);
+    m.dout = mods[i].dim;
+    m.row_off = mods[i].row_offset;
+    m.tile0 = tiles;
+    m.K = mods[i].n_bases;
+    m.act = mods[i].activation;
+    tiles += ceil_div(mods[i].dim, kPN);
+  }
+  a.n_tiles = tiles;
   a.pair_tiles = ceil_div(a.m_tiles, int64_t{2}) * a.n_tiles;
-  if (a.n_tokens == 0 || p.dim == 0) return MOC_OK;
-  const bool act = p.activation != 0;
-#define MOC_PROJ_CASE(s) \
-  if (p.kernel_size == s) return act ? proj_inst<s, true>(p, a, st) : proj_inst<s, false>(p, a, st);
-  MOC_PROJ_CASE(1) MOC_PROJ_CASE(2) MOC_PROJ_CASE(3) MOC_PROJ_CASE(4)
-  MOC_PROJ_CASE(5) MOC_PROJ_CASE(6) MOC_PROJ_CASE(7) MOC_PROJ_CASE(8)
-#undef MOC_PROJ_CASE
-  return MOC_ERR_UNSUPPORTED_SHAPE;
+  if (a.n_tokens == 0 || tiles == 0) return MOC_OK;
+  switch (S) {
+    case 1: return proj_inst<1>(a, h, weight, weight_rows, st);
+    case 2: return proj_inst<2>(a, h, weight, weight_rows, st);
+    case 3: return proj_inst<3>(a, h, weight, weight_rows, st);
+    case 4: return proj_inst<4>(a, h, weight, weight_rows, st);
+    case 5: return proj_inst<5>(a, h, weight, weight_rows, st);
+    case 6: return proj_inst<6>(a, h, weight, weight_rows, st);
+    case 7: return proj_inst<7>(a, h, weight, weight_rows, st);
+    case 8: return proj_inst<8>(a, h, weight, weight_rows, st);
+    default: return MOC_ERR_UNSUPPORTED_SHAPE;
+  }
 }
 
 int proj_status(int* out, bool clear) {

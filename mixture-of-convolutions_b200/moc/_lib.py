@@ -69,6 +69,23 @@ class MocDecodeModule(ctypes.Structure):
 DECODE_MAX_MODULES = 4
 
 
+class MocProjModule(ctypes.Structure):
+    """Mirror of ``struct moc_proj_module``."""
+
+    _fields_ = [
+        ("dim", ctypes.c_int64),
+        ("row_offset", ctypes.c_int64),
+        ("n_bases", ctypes.c_int32),
+        ("activation", ctypes.c_int32),
+        ("alpha", ctypes.c_void_p),
+        ("basis", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+    ]
+
+
+PROJ_MAX_MODULES = 4
+
+
 class MocProjProblem(ctypes.Structure):
     """Mirror of ``struct moc_proj_problem``."""
 
@@ -123,6 +140,8 @@ SIGNATURES = {
     "moc_prepare_chunk_indices": (ctypes.c_int, [_P, _I32, _I64, _I32, _P, _I64, _P]),
     "moc_decode_step_multi": (ctypes.c_int, [_I32, ctypes.POINTER(MocDecodeModule), _I64, _I64, _P, _P]),
     "moc_proj_forward": (ctypes.c_int, [ctypes.POINTER(MocProjProblem), _P]),
+    "moc_proj_forward_multi": (ctypes.c_int, [_I32, ctypes.POINTER(MocProjModule), _I64, _I64, _I64, _I32, _P, _P,
+                                              _I64, _P]),
     "moc_comm_create": (ctypes.c_int, [_I32, _I32, _I64, ctypes.POINTER(_P), _P]),
     "moc_comm_connect": (ctypes.c_int, [_P, _P]),
     "moc_comm_allreduce": (ctypes.c_int, [_P, _I32, ctypes.POINTER(_P), ctypes.POINTER(_I64), ctypes.POINTER(_I32), _P]),

@@ -113,6 +113,70 @@ def decode_step(modules: Sequence[MoC], xs: Sequence[torch.Tensor], z: torch.Ten
     return [y.reshape(xo.shape) for y, xo in zip(ys, xs)]
 
 
+def _proj_alpha(h: torch.Tensor, module: MoC, z: torch.Tensor | None, alpha: torch.Tensor | None) -> torch.Tensor:
+    B, T = h.shape[:2]
+    from . import ops
+
+    if alpha is None:
+        if z is None or z.shape[:2] != (B, T):
+            raise ValueError(f"z must be [{B}, {T}, z_dim], got {None if z is None else tuple(z.shape)}")
+        alpha = ops.launch_router_forward(z.detach(), module.router.detach(), module.router_activation)
+    if alpha.shape != (B, T, module.k) or alpha.dtype != torch.bfloat16:
+        raise ValueError(f"alpha must be bf16 [{B}, {T}, {module.k}], got {tuple(alpha.shape)} {alpha.dtype}")
+    return _aligned(alpha.detach())
+
+
+def proj_forward_multi(h: torch.Tensor, weight: torch.Tensor, modules: Sequence[MoC], z: torch.Tensor | None = None,
+                       alphas: Sequence[torch.Tensor] | None = None) -> list[torch.Tensor]:
+    """The reference's attention-block pattern (README.md:115-129) in one kernel:
+
+        q, k, v = qkv_proj(x_norm).split([q_dim, k_dim, v_dim], dim=-1)
+        q, _ = q_conv(q, x_norm); k, _ = k_conv(k, x_norm); v, _ = v_conv(v, x_norm)
+
+    h:       [B, T, in_dim] bf16 (x_norm), fixed-length sequences (no cache, no packing).
+    weight:  [sum of module dims, in_dim] bf16 (qkv_proj.weight), module i's rows following
+             module i-1's.
+    modules: up to four bf16 MoC modules with one kernel size (K % 8 == 0, K <= 16).
+    z:       the routing input for every module, or ``alphas``: each module's router output.
+
+    h is read once for all modules; each module's projection is rounded to bf16 and
+    convolved on chip.  Forward only (no autograd graph).  Returns the modules' outputs."""
+    if not 1 <= len(modules) <= _lib.PROJ_MAX_MODULES:
+        raise ValueError(f"proj_forward_multi takes 1 to {_lib.PROJ_MAX_MODULES} modules, got {len(modules)}")
+    if h.ndim != 3 or h.dtype != torch.bfloat16 or not h.is_cuda:
+        raise ValueError(f"h must be a CUDA bf16 tensor [B, T, in_dim], got {tuple(h.shape)} {h.dtype}")
+    B, T, Dm = h.shape
+    rows = sum(m.dim for m in modules)
+    if weight.shape != (rows, Dm) or weight.dtype != torch.bfloat16:
+        raise ValueError(f"weight must be bf16 [{rows}, {Dm}], got {tuple(weight.shape)} {weight.dtype}")
+    if any(not isinstance(m, MoC) or m.conv_bases.dtype != torch.bfloat16 for m in modules):
+        raise ValueError("proj_forward_multi needs bf16 moc.MoC modules")
+    if len({m.kernel_size for m in modules}) != 1:
+        raise ValueError("all modules must have one kernel_size")
+    if (alphas is None) == (z is None):
+        raise ValueError("pass exactly one of z (routing input) or alphas (router outputs)")
+    if alphas is not None and len(alphas) != len(modules):
+        raise ValueError("one alpha per module")
+    h2, w2 = _aligned(h.detach()), _aligned(weight.detach())
+    keep, outs = [h2, w2], []
+    arr = (_lib.MocProjModule * len(modules))()
+    off = 0
+    for i, m in enumerate(modules):
+        a2 = _proj_alpha(h, m, z, None if alphas is None else alphas[i])
+        basis = _aligned(m.conv_bases.detach())
+        out = torch.empty(B, T, m.dim, dtype=torch.bfloat16, device=h.device)
+        keep += [a2, basis]
+        outs.append(out)
+        arr[i] = _lib.MocProjModule(dim=m.dim, row_offset=off, n_bases=m.k, activation=int(m.activation is not None),
+                                    alpha=a2.data_ptr(), basis=basis.data_ptr(), out=out.data_ptr())
+        off += m.dim
+    with torch.cuda.device(h.device):
+        rc = _lib.load().moc_proj_forward_multi(len(modules), arr, B, T, Dm, modules[0].kernel_size, h2.data_ptr(),
+                                                w2.data_ptr(), rows, _lib.stream_of(h.device))
+    _lib.check(rc, "moc_proj_forward_multi")
+    return outs
+
+
 def proj_forward(h: torch.Tensor, weight: torch.Tensor, module: MoC, z: torch.Tensor | None = None,
                  alpha: torch.Tensor | None = None) -> torch.Tensor:
     """``module(h @ weight.T, z)[0]`` in one kernel: the projection runs on the tensor cores and
@@ -135,15 +199,8 @@ def proj_forward(h: torch.Tensor, weight: torch.Tensor, module: MoC, z: torch.Te
         raise ValueError("proj_forward needs a bf16 module")
     if (alpha is None) == (z is None):
         raise ValueError("pass exactly one of z (routing input) or alpha (router output)")
-    from . import ops
-
-    if alpha is None:
-        if z.shape[:2] != (B, T):
-            raise ValueError(f"z must be [{B}, {T}, z_dim], got {tuple(z.shape)}")
-        alpha = ops.launch_router_forward(z.detach(), module.router.detach(), module.router_activation)
-    if alpha.shape != (B, T, module.k) or alpha.dtype != torch.bfloat16:
-        raise ValueError(f"alpha must be bf16 [{B}, {T}, {module.k}], got {tuple(alpha.shape)} {alpha.dtype}")
-    h2, w2, a2 = _aligned(h.detach()), _aligned(weight.detach()), _aligned(alpha.detach())
+    a2 = _proj_alpha(h, module, z, alpha)
+    h2, w2 = _aligned(h.detach()), _aligned(weight.detach())
     basis = _aligned(module.conv_bases.detach())
     out = torch.empty(B, T, module.dim, dtype=torch.bfloat16, device=h.device)
     prob = _lib.MocProjProblem(batch=B, seq_len=T, in_dim=Dm, dim=module.dim, n_bases=module.k,

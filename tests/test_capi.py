@@ -127,7 +127,8 @@ def _c_layout(struct: str, fields: list[str]) -> dict[str, int]:
 
 @pytest.mark.parametrize("struct,mirror", [("moc_problem", _lib.MocProblem),
                                            ("moc_decode_module", _lib.MocDecodeModule),
-                                           ("moc_proj_problem", _lib.MocProjProblem)])
+                                           ("moc_proj_problem", _lib.MocProjProblem),
+                                           ("moc_proj_module", _lib.MocProjModule)])
 def test_ctypes_structs_match_the_header_layout(struct, mirror):
     names = [f[0] for f in mirror._fields_]
     layout = _c_layout(struct, names)
@@ -185,6 +186,36 @@ def test_proj_checks():
     assert lib.moc_proj_forward(prob(weight=0), None) == 1
     assert lib.moc_proj_forward(prob(out=1288), None) == 4      # 16-byte alignment
     assert lib.moc_proj_forward(prob(batch=0), None) == 0       # no tokens: no work
+
+
+def test_proj_multi_checks():
+    lib = _lib.load()
+
+    def mods(n, **kw):
+        arr = (_lib.MocProjModule * n)()
+        for i in range(n):
+            f = dict(dim=128, row_offset=128 * i, n_bases=16, activation=0, alpha=256, basis=512, out=768)
+            f.update(kw)
+            arr[i] = _lib.MocProjModule(**f)
+        return arr
+
+    def call(n, m, rows=384, **kw):
+        f = dict(batch=2, seq_len=64, in_dim=256, kernel_size=4, h=1024, weight=1280)
+        f.update(kw)
+        return lib.moc_proj_forward_multi(n, m, f["batch"], f["seq_len"], f["in_dim"], f["kernel_size"], f["h"],
+                                          f["weight"], rows, None)
+
+    assert call(0, mods(1)) == 1
+    assert call(5, mods(5)) == 1                       # at most 4 modules
+    assert call(3, mods(3), rows=300) == 1             # rows past the weight
+    assert call(1, mods(1, row_offset=-8)) == 1
+    assert call(1, mods(1, n_bases=24)) == 3
+    assert call(1, mods(1, dim=100)) == 3
+    assert call(1, mods(1), kernel_size=9) == 3
+    assert call(1, mods(1, activation=3)) == 1
+    assert call(1, mods(1, out=776)) == 4              # 16-byte alignment
+    assert call(1, mods(1), h=1032) == 4
+    assert call(3, mods(3), batch=0) == 0              # no tokens: no work
 
 
 def test_comm_checks():

@@ -78,3 +78,33 @@ def test_proj_is_deterministic():
     a = fused.proj_forward(h, w, m, z=h)
     b = fused.proj_forward(h, w, m, z=h)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dims,acts", [((512, 128, 128), (None, None, None)),
+                                       ((256, 200, 64), ("silu", None, "silu")),
+                                       ((384,), (None,))])
+def test_proj_multi_matches_per_module_calls(dims, acts):
+    """One launch over the concatenated weight gives each module bitwise what its own
+    moc_proj_forward gives (same tiles, same sums)."""
+    torch.manual_seed(5)
+    B, T, Dm, S = 2, 250, 256, 4
+    g = torch.Generator().manual_seed(6)
+    mods = []
+    for D, act in zip(dims, acts):
+        m = MoC(dim=D, z_dim=Dm, kernel_size=S, k=16, activation=act, init_std=0.1, router_activation="exp")
+        with torch.no_grad():
+            m.router.copy_(torch.randn(16, Dm, generator=g) * 0.05)
+        mods.append(m.to(device="cuda", dtype=torch.bfloat16))
+    h = torch.randn(B, T, Dm, generator=g).bfloat16().cuda()
+    w = (torch.randn(sum(dims), Dm, generator=g) / Dm ** 0.5).bfloat16().cuda()
+    ys = fused.proj_forward_multi(h, w, mods, z=h)
+    off = 0
+    for m, y, D in zip(mods, ys, dims):
+        ref = fused.proj_forward(h, w[off:off + D], m, z=h)
+        assert torch.equal(y, ref)
+        y2, _ = m(h @ w[off:off + D].T, h)
+        assert rel_err(y, y2.detach()) <= TOL
+        off += D
+    assert _lib.device_status(clear=True) == 0
+    with pytest.raises(ValueError):
+        fused.proj_forward_multi(h, w[:-8], mods, z=h)  # weight rows != sum of dims
