@@ -14,6 +14,37 @@ namespace moc {
 
 using bf16 = __nv_bfloat16;
 
+// ---------------------------------------------------------------- programmatic dependent launch
+//
+// The kernels of a training step are launched as programmatic dependents of the kernel
+// before them on the stream (launch_pdl): a kernel may start while its predecessor
+// finishes, runs its set-up (shared memory, barriers, tensor-map prefetch, loads of the
+// basis / router weight, which no kernel of the chain writes) and then waits in
+// griddep_wait() for the predecessor grid to complete, with its writes visible.  Every
+// read of an activation, gradient or partial sum, and every global write, comes after that
+// wait, so no kernel touches memory a running predecessor may still use (including memory
+// the caching allocator handed out again).  Each kernel lets its own dependent start at
+// once (griddep_launch_dependents); the dependent still waits for it to complete.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // ---------------------------------------------------------------- conversions
 
 __device__ __forceinline__ float to_f32(float v) { return v; }

@@ -81,6 +81,7 @@ __global__ void __launch_bounds__(128) k_router_fwd_tc(const __grid_constant__ C
     for (int st = 0; st < kFwdStages; ++st) mbar_init(bar0 + 8 * st, 1);
     fence_mbar_init();
   }
+  griddep_wait();  // z may come from the kernels before this one
   __syncthreads();
   if (threadIdx.x == 0)
     for (int c = 0; c < kFwdStages && c < n_chunks; ++c) issue(c);
@@ -121,6 +122,7 @@ __global__ void __launch_bounds__(128) k_router_fwd_tc(const __grid_constant__ C
     __syncthreads();  // every warp is done with this stage before it is refilled
     if (threadIdx.x == 0 && c + kFwdStages < n_chunks) issue(c + kFwdStages);
   }
+  griddep_launch_dependents();  // only the epilogue is left
 
   // acc[kn][2h + e] = logit(token warp*16 + g + 8h, base 8kn + 2q + e); the 4 lanes of a
   // quad hold one token row.
@@ -256,6 +258,7 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
       cp_async16(smem_addr(w_s + k * kRowB + chunk * 16), ok ? a.w + k * a.Dz + col : a.w, ok ? 16u : 0u);
     }
     cp_async_commit();
+    griddep_wait();  // z, alpha and dalpha may come from the kernels before this one
     __syncthreads();
     if (threadIdx.x == 0) issue(i0, 0);
     cp_async_wait<0>();
@@ -264,6 +267,7 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
     for (int kt = 0; kt < KT; ++kt)
       ldsm_x4_t(smem_addr(w_s + (kt * 16 + lm_row(lane)) * kRowB + (cw + lm_col(lane)) * 2), wb[kt]);
   }
+  if (i0 >= i1) griddep_wait();  // a CTA without tiles still writes its (zero) dW partial
   // alpha / dalpha of the next tile are loaded one iteration ahead into registers: four
   // threads per token, each owning KP/4 bases
   constexpr int KQ = KP / 4;
@@ -402,6 +406,7 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
       }
     }
   }
+  griddep_launch_dependents();  // only the dW partial store is left
   if (want_dw) {
     const int64_t grp = blockIdx.y;
 #pragma unroll
@@ -416,6 +421,7 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
 }
 
 __global__ void k_sum_groups(const float* __restrict__ part, int64_t groups, int64_t n, void* out, int dtype) {
+  griddep_wait();  // the partials of the backward kernel
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float s = 0.f;
@@ -423,6 +429,7 @@ __global__ void k_sum_groups(const float* __restrict__ part, int64_t groups, int
     for (int64_t g = 0; g < groups; ++g) s += __ldg(part + g * n + i);
     st_any(out, dtype, i, s);
   }
+  griddep_launch_dependents();
 }
 
 int sm_count_r() {
@@ -466,10 +473,10 @@ int fwd_kt(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, 
   rc = make_tmap_bf16_2d(&wmap, w, static_cast<uint64_t>(Dz), static_cast<uint64_t>(K), static_cast<uint64_t>(Dz) * 2,
                          64, KT * 16);
   if (rc != MOC_OK) return rc;
-  k_router_fwd_tc<KT><<<static_cast<unsigned>(ceil_div(N, kFwdRows)), 128, FwdLayout<KT>::total, st>>>(
-      zmap, wmap, static_cast<bf16*>(alpha), N, Dz, K, act);
+  const cudaError_t e = launch_pdl(k_router_fwd_tc<KT>, dim3(static_cast<unsigned>(ceil_div(N, kFwdRows))), dim3(128),
+                                   FwdLayout<KT>::total, st, zmap, wmap, static_cast<bf16*>(alpha), N, Dz, K, act);
   note_launch();
-  return note_cuda(cudaGetLastError());
+  return note_cuda(e);
 }
 
 template <int KT>
@@ -481,16 +488,18 @@ int bwd_kt(RouterBwdArgs& a, const void* z, int64_t slices, int64_t groups, void
   rc = make_tmap_bf16_2d(&zmap, z, static_cast<uint64_t>(a.Dz), static_cast<uint64_t>(a.N),
                          static_cast<uint64_t>(a.Dz) * 2, 64, kBwdTile);
   if (rc != MOC_OK) return rc;
-  k_router_bwd_tc<KT><<<dim3(static_cast<unsigned>(slices), static_cast<unsigned>(groups)), 256,
-                        BwdLayout<KT>::total, st>>>(zmap, a);
+  cudaError_t e = launch_pdl(k_router_bwd_tc<KT>, dim3(static_cast<unsigned>(slices), static_cast<unsigned>(groups)),
+                             dim3(256), BwdLayout<KT>::total, st, zmap, a);
   note_launch();
+  if (e != cudaSuccess) return note_cuda(e);
   if (dw != nullptr) {
     const int64_t n = static_cast<int64_t>(a.K) * a.Dz;
     const int64_t blocks = std::min<int64_t>(ceil_div(n, 256), 4 * sm_count_r());
-    k_sum_groups<<<static_cast<unsigned>(blocks), 256, 0, st>>>(a.dw_part, groups, n, dw, MOC_DTYPE_BF16);
+    e = launch_pdl(k_sum_groups, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, a.dw_part, groups, n, dw,
+                   static_cast<int>(MOC_DTYPE_BF16));
     note_launch();
   }
-  return note_cuda(cudaGetLastError());
+  return note_cuda(e);
 }
 
 }  // namespace

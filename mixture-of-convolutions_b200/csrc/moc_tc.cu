@@ -211,6 +211,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
   }
   load_basis<L, false>(a, sm.head, ch_base, S);
   cp_async_commit();
+  griddep_wait();  // x and alpha may come from the kernels before this one
   __syncthreads();
   if (threadIdx.x == 0) {
     int64_t ss, se, r0, r1;
@@ -260,6 +261,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
           ldsm_x4_t(smem_addr(sm.head + (s * L::KP + kt * 16 + lrow) * kRowB + (warp * 16 + lm_col(lane)) * 2),
                     bw[s][kt]);
     }
+    if (it + 1 == i1) griddep_launch_dependents();  // the CTA's last item
     int64_t ss, se, r0, r1;
     if (a.rm.item(it, ss, se, r0, r1)) {
       char* stage_p = sm.stages_p + cur * L::stage_bytes;
@@ -383,6 +385,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
     }
     load_basis<L, true>(a, basis_s, ch_base, S);
     cp_async_commit();
+    griddep_wait();  // x, dy and alpha may come from the kernels before this one
     __syncthreads();
     if (threadIdx.x == 0) {
       int64_t ss, se, r0, r1;
@@ -391,6 +394,8 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       else
         mbar_arrive(sm.bar);
     }
+  } else {
+    griddep_wait();  // a CTA without items still writes its (zero) dbasis partial
   }
   for (int64_t it = i0; it < i1; ++it) {
     const int cur = static_cast<int>((it - i0) & 1);
@@ -648,6 +653,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
     // the next iteration's wait barrier orders these reads of red_s and the stage before reuse
   }
 
+  griddep_launch_dependents();  // only the dbasis partial store is left
   // dbasis partial of this CTA: db_part[group][k][s][ch]
   if constexpr (!DB) return;
   const int64_t grp = blockIdx.y;
@@ -667,6 +673,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
 __global__ void k_tc_finalize(const float* __restrict__ da_part, int64_t n_slices, int64_t nk, void* dalpha,
                               int adt, const float* __restrict__ db_part, int64_t groups, int64_t ksd, void* dbasis,
                               int bdt) {
+  griddep_wait();  // the partials of the backward kernel
   const int64_t total = nk + ksd;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -682,6 +689,7 @@ __global__ void k_tc_finalize(const float* __restrict__ da_part, int64_t n_slice
       st_any(dbasis, bdt, j, s);
     }
   }
+  griddep_launch_dependents();
 }
 
 // ------------------------------------------------------------------ host side
@@ -753,10 +761,10 @@ int fwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alph
   Maps m;
   rc = make_maps<L, false>(p, x, nullptr, alpha, m);
   if (rc != MOC_OK) return rc;
-  k_tc_fwd<KT, S, ACT><<<dim3(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups)), kThreads, L::total,
-                         st>>>(m.x, m.a, args);
+  const cudaError_t e = launch_pdl(k_tc_fwd<KT, S, ACT>, dim3(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups)),
+                                   dim3(kThreads), L::total, st, m.x, m.a, args);
   note_launch();
-  return note_cuda(cudaGetLastError());
+  return note_cuda(e);
 }
 
 template <int KT, int S, bool ACT>
@@ -789,23 +797,22 @@ int bwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alph
   if (rc != MOC_OK) return rc;
   const dim3 grid(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups));
   if constexpr (bwd_split(KT, S)) {
-    k_tc_bwd<KT, S, ACT, kBwdDxDa><<<grid, kThreads, L::total, st>>>(m.x, m.dy, m.a, args);
+    rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdDxDa>, grid, dim3(kThreads), L::total, st, m.x, m.dy, m.a, args));
     note_launch();
-    rc = note_cuda(cudaGetLastError());
     if (rc != MOC_OK) return rc;
-    k_tc_bwd<KT, S, ACT, kBwdDb><<<grid, kThreads, Layout<KT, S, ACT, true, kBwdDb>::total, st>>>(m.x, m.dy, m.a,
-                                                                                                  args);
+    rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdDb>, grid, dim3(kThreads), Layout<KT, S, ACT, true, kBwdDb>::total,
+                              st, m.x, m.dy, m.a, args));
   } else {
-    k_tc_bwd<KT, S, ACT, kBwdAll><<<grid, kThreads, L::total, st>>>(m.x, m.dy, m.a, args);
+    rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdAll>, grid, dim3(kThreads), L::total, st, m.x, m.dy, m.a, args));
   }
   note_launch();
-  rc = note_cuda(cudaGetLastError());
   if (rc != MOC_OK) return rc;
   const int64_t blocks = std::min<int64_t>(ceil_div(nk + ksd, 256), 8 * sm_count());
-  k_tc_finalize<<<static_cast<unsigned>(blocks), 256, 0, st>>>(args.da_part, pl.slices, nk, dalpha, p.alpha_dtype,
-                                                               args.db_part, pl.groups, ksd, dbasis, p.basis_dtype);
+  const cudaError_t e = launch_pdl(k_tc_finalize, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, args.da_part,
+                                   pl.slices, nk, dalpha, p.alpha_dtype, args.db_part, pl.groups, ksd, dbasis,
+                                   p.basis_dtype);
   note_launch();
-  return note_cuda(cudaGetLastError());
+  return note_cuda(e);
 }
 
 template <template <int, int, bool> class F, typename... Args>
