@@ -241,7 +241,9 @@ def _canonicalize_packed_input(
     if x.ndim == 2 and alpha.ndim == 2:
         return x, alpha, False
     if x.ndim == 3 and alpha.ndim == 3 and x.shape[0] == 1 and alpha.shape[0] == 1:
-        return x[0], alpha[0], True
+        # views, as the reference's squeeze(0) (moc/api.py:204-205): their backward is a view
+        # too, where x[0]'s would zero-fill a [1, N, D] gradient and copy dx into it
+        return x.squeeze(0), alpha.squeeze(0), True
     raise ValueError("varlen x/alpha must be [N,D]/[N,K] or [1,N,D]/[1,N,K]")
 
 
