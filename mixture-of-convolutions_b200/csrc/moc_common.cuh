@@ -114,6 +114,27 @@ __device__ __forceinline__ float dsilu_bf(float v) {
   return sig * fmaf(v, 1.0f - sig, 1.0f);
 }
 
+// The same for a pair of values with packed fp32x2 arithmetic: with h = v / 2,
+// silu(v) = h + h tanh(h), and sigmoid(v) = 1/2 + tanh(h) / 2.
+__device__ __forceinline__ float2 tanh2_approx(float2 h) {
+  float2 t;
+  asm("tanh.approx.f32 %0, %1;\n" : "=f"(t.x) : "f"(h.x));
+  asm("tanh.approx.f32 %0, %1;\n" : "=f"(t.y) : "f"(h.y));
+  return t;
+}
+__device__ __forceinline__ float2 silu_bf2(float v0, float v1) {
+  const float2 h = __fmul2_rn(make_float2(v0, v1), make_float2(0.5f, 0.5f));
+  return __ffma2_rn(h, tanh2_approx(h), h);
+}
+// dsilu(v) = sig (1 + v (1 - sig))
+__device__ __forceinline__ float2 dsilu_bf2(float v0, float v1) {
+  const float2 v = make_float2(v0, v1), half = make_float2(0.5f, 0.5f);
+  const float2 t = tanh2_approx(__fmul2_rn(v, half));
+  const float2 sig = __ffma2_rn(t, half, half);
+  const float2 one_m = __ffma2_rn(t, make_float2(-0.5f, -0.5f), half);
+  return __fmul2_rn(sig, __ffma2_rn(v, one_m, make_float2(1.f, 1.f)));
+}
+
 // ------------------------------------------------------------------ row mapping
 
 // A work item is a run of consecutive token rows [r0, r1) inside one sequence whose

@@ -483,8 +483,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             const int nt = i >> 1, h = i & 1;
             float v0 = acc[nt][2 * h], v1 = acc[nt][2 * h + 1];
             if (act) {
-              v0 = silu_bf(v0);
-              v1 = silu_bf(v1);
+              const float2 sv = silu_bf2(v0, v1);
+              v0 = sv.x;
+              v1 = sv.y;
             }
             o[i] = pack_bf16(v0, v1);
           }

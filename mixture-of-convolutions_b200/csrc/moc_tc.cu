@@ -313,8 +313,9 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
           const int nt = i >> 1, h = i & 1;
           float v0 = acc[nt][2 * h], v1 = acc[nt][2 * h + 1];
           if (ACT) {
-            v0 = silu_bf(v0);
-            v1 = silu_bf(v1);
+            const float2 sv = silu_bf2(v0, v1);
+            v0 = sv.x;
+            v1 = sv.y;
           }
           o[i] = pack_bf16(v0, v1);
         }
@@ -524,8 +525,8 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
               const uint32_t d = *reinterpret_cast<const uint32_t*>(
                   stage_p + dy_box + row * 128 + (((chunk ^ row) & 7) << 4) + 4 * q);
               float2 o;
-              o.x = bf_lo(d) * dsilu_bf(pre[nt][2 * h]);
-              o.y = bf_hi(d) * dsilu_bf(pre[nt][2 * h + 1]);
+              const float2 ds = dsilu_bf2(pre[nt][2 * h], pre[nt][2 * h + 1]);
+              o = __fmul2_rn(make_float2(bf_lo(d), bf_hi(d)), ds);
               *reinterpret_cast<float2*>(dz_s + row * kDzRowB + (ch_w + nt * 8 + 2 * q) * 4) = o;
             }
         }
