@@ -35,7 +35,6 @@ constexpr int kTile = 64;              // token rows per work item
 constexpr int kBD = 128;               // channels per CTA (two 64-channel TMA boxes)
 constexpr int kThreads = 256;          // 8 warps x 16 channels
 constexpr int kRowB = (kBD + 8) * 2;   // basis row in smem: 272 B (16 B pad: conflict-free ldmatrix)
-constexpr int kDzRowB = (kBD + 8) * 4; // fp32 dz row: 544 B
 constexpr int kHalo = 8;               // past-halo rows kept before each tile (S - 1 <= 7)
 constexpr int kFut = 16;               // future rows kept after each tile (S - 1 <= 7, one 16-row block)
 
@@ -71,20 +70,22 @@ struct Layout {
   static constexpr int basis_bytes = S * KP * kRowB;
   // dalpha partials of RB 16-row blocks x 8 warps, reduced across warps once per RB blocks
   // (with the basis staged beside them at 32 bases and more than 4 taps: one block)
-  static constexpr int RB = (KT == 1 || BREG) ? 4 : (S > 4 ? 1 : 2);
+  // (SiLU backward at one base group: two, so that two CTAs fit an SM)
+  static constexpr int RB = (KT == 1 || BREG) ? ((BWD && ACT) ? 2 : 4) : (S > 4 ? 1 : 2);
   static constexpr int red_bytes = (BWD && PART != kBwdDb) ? RB * 8 * 16 * KP * 4 : 0;
   // with register-resident basis fragments the basis staging area is reused for the
   // dalpha reduction buffer once the fragments are loaded
   static constexpr int head_bytes =
       align1k((BWD && BREG) ? (basis_bytes > red_bytes ? basis_bytes : red_bytes) : basis_bytes + red_bytes);
-  static constexpr int dz_bytes = (BWD && ACT) ? FR * kDzRowB : 0;
+  // the SiLU backward writes dz in place of dy (bf16, same swizzled tile): no staging of its own
+  static constexpr int dz_bytes = 0;
   // per-warp output staging: one 16-row x 16-channel bf16 block (32-byte rows)
   static constexpr int ost_bytes = BWD ? 0 : 8 * 16 * 32;
   static constexpr int total = 1024 + 2 * stage_bytes + head_bytes + dz_bytes + ost_bytes + 64;
   // forward at 32 bases and more than 4 taps: its 68 KB basis staging leaves room for at
   // most two CTAs anyway, and the 64 basis fragment registers need more than 128 per thread
   static constexpr int min_blocks =
-      BWD ? ((BREG && !ACT && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 3 : (KT * S > 8 ? 1 : 2));
+      BWD ? ((BREG && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 3 : (KT * S > 8 ? 1 : 2));
 };
 
 struct TcArgs {
@@ -348,7 +349,6 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
   const Smem<L> sm(smem_raw);
   char* basis_s = sm.head;
   float* red_s = reinterpret_cast<float*>(sm.head + (BREG ? 0 : L::basis_bytes));  // [RB][8 warps][16][KP]
-  char* dz_s = sm.dz;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int64_t slice = blockIdx.x;
@@ -483,21 +483,11 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
         }
       }
     };
-    // fp32 dz (SiLU path) in the C layout: v[nt][2h + e] at (row rb + g + 8h, ch 8nt + 2q + e)
-    auto load_dz32 = [&](int rb, float (&v)[2][4]) {
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float2 d =
-              *reinterpret_cast<const float2*>(dz_s + (rb + g + 8 * h) * kDzRowB + (ch_w + nt * 8 + 2 * q) * 4);
-          v[nt][2 * h] = d.x;
-          v[nt][2 * h + 1] = d.y;
-        }
-    };
 
     if (valid) {
-      // ---- phase 1 (SiLU): dz = dy * silu'(pre) for tile rows 0..79 (future rows feed dx)
+      // ---- phase 1 (SiLU): dz = dy * silu'(pre) for tile rows 0..79 (future rows feed dx),
+      // rounded to bf16 and written over dy in the stage (each lane its own pairs), so phase 2
+      // is the plain backward on dz
       if constexpr (ACT) {
         for (int b = 0; b < 5; ++b) {
           float pre[2][4] = {};
@@ -522,12 +512,10 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
             for (int h = 0; h < 2; ++h) {
               const int row = 16 * b + g + 8 * h;
               const int chunk = 2 * (warp & 3) + nt;  // 16-byte chunk of (row, ch_w + 8nt)
-              const uint32_t d = *reinterpret_cast<const uint32_t*>(
-                  stage_p + dy_box + row * 128 + (((chunk ^ row) & 7) << 4) + 4 * q);
-              float2 o;
+              uint32_t* d = reinterpret_cast<uint32_t*>(stage_p + dy_box + row * 128 + (((chunk ^ row) & 7) << 4) + 4 * q);
               const float2 ds = dsilu_bf2(pre[nt][2 * h], pre[nt][2 * h + 1]);
-              o = __fmul2_rn(make_float2(bf_lo(d), bf_hi(d)), ds);
-              *reinterpret_cast<float2*>(dz_s + row * kDzRowB + (ch_w + nt * 8 + 2 * q) * 4) = o;
+              const float2 o = __fmul2_rn(make_float2(bf_lo(*d), bf_hi(*d)), ds);
+              *d = pack_bf16(o.x, o.y);
             }
         }
         __syncwarp();
@@ -543,13 +531,8 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
 #pragma unroll
         for (int kt = 0; kt < KT; ++kt) ldsm_x4_t(a_s + (16 * b) * L::ARB + kt * 32 + a_lane, ab[kt]);
       }
-      uint32_t dyu[4];  // dy of this block, packed bf16 pairs (no activation)
-      float dzu[2][4];  // fp32 dz of this block (SiLU)
-      if constexpr (ACT) {
-        load_dz32(16 * b, dzu);
-      } else {
-        ldsm_x4(dy_addr(16 * b), dyu);
-      }
+      uint32_t dyu[4];  // dz (= dy without SiLU) of this block, packed bf16 pairs
+      ldsm_x4(dy_addr(16 * b), dyu);
       float dxa[2][4] = {};
       float daa[2 * KT][4] = {};
 #pragma unroll
@@ -558,36 +541,19 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
         if (want_dx) {
           float w[2][4];
           w_frag(16 * b + j, s, w);  // W at rows t + j
-          if constexpr (ACT) {
-            float dzs[2][4];
-            load_dz32(16 * b + j, dzs);
+          uint32_t dys[4];
+          ldsm_x4(dy_addr(16 * b + j), dys);
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-              ffma2(dxa[nt][0], dxa[nt][1], w[nt][0], w[nt][1], dzs[nt][0], dzs[nt][1]);
-              ffma2(dxa[nt][2], dxa[nt][3], w[nt][2], w[nt][3], dzs[nt][2], dzs[nt][3]);
-            }
-          } else {
-            uint32_t dys[4];
-            ldsm_x4(dy_addr(16 * b + j), dys);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-              ffma2(dxa[nt][0], dxa[nt][1], w[nt][0], w[nt][1], bf_lo(dys[2 * nt]), bf_hi(dys[2 * nt]));
-              ffma2(dxa[nt][2], dxa[nt][3], w[nt][2], w[nt][3], bf_lo(dys[2 * nt + 1]), bf_hi(dys[2 * nt + 1]));
-            }
+          for (int nt = 0; nt < 2; ++nt) {
+            ffma2(dxa[nt][0], dxa[nt][1], w[nt][0], w[nt][1], bf_lo(dys[2 * nt]), bf_hi(dys[2 * nt]));
+            ffma2(dxa[nt][2], dxa[nt][3], w[nt][2], w[nt][3], bf_lo(dys[2 * nt + 1]), bf_hi(dys[2 * nt + 1]));
           }
         }
         uint32_t xr[4];
         ldsm_x4(x_addr(kHalo + 16 * b - j), xr);
         uint32_t m[4];  // A operand (tokens x channels) of dalpha, rounded to bf16
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          if constexpr (ACT) {
-            const int nt = r >> 1, h = r & 1;
-            m[r] = pack_bf16(dzu[nt][2 * h] * bf_lo(xr[r]), dzu[nt][2 * h + 1] * bf_hi(xr[r]));
-          } else {
-            m[r] = hmul2_bf16(dyu[r], xr[r]);
-          }
-        }
+        for (int r = 0; r < 4; ++r) m[r] = hmul2_bf16(dyu[r], xr[r]);
         if constexpr (DXDA) {
 #pragma unroll
           for (int kt = 0; kt < KT; ++kt) {
@@ -773,7 +739,7 @@ int bwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alph
              void* dbasis, cudaStream_t st) {
   // the layout of the launch (of the first pass when split); both passes share one plan
   using L = Layout<KT, S, ACT, true, bwd_split(KT, S) ? kBwdDxDa : kBwdAll>;
-  static_assert(L::min_blocks == ((L::BREG && !ACT && KT == 1) ? 2 : 1), "bwd_min_blocks() mirrors Layout::min_blocks");
+  static_assert(L::min_blocks == ((L::BREG && KT == 1) ? 2 : 1), "bwd_min_blocks() mirrors Layout::min_blocks");
   const Plan pl = make_plan(p, L::min_blocks);
   args.rm = pl.rm;
   args.items_per_group = pl.ipg;
@@ -853,7 +819,7 @@ bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u
 int bwd_min_blocks(const moc_problem& p) {
   const int kt = p.n_bases <= 16 ? 1 : 2;
   const bool breg = kt * p.kernel_size <= 4;
-  return (breg && p.activation == 0 && kt == 1) ? 2 : 1;
+  return (breg && kt == 1) ? 2 : 1;
 }
 
 void ws_split(const moc_problem& p, int64_t& slices, int64_t& groups, size_t& da_bytes, size_t& db_bytes) {
