@@ -524,10 +524,10 @@ int proj_inst(ProjArgs& args, const void* h, const void* weight, int64_t weight_
   }
   CUtensorMap hmap, wmap;
   int rc = make_tmap_bf16_2d(&hmap, h, static_cast<uint64_t>(args.dm), static_cast<uint64_t>(args.n_tokens),
-                             static_cast<uint64_t>(args.dm) * 2, kPK, kPM, true);
+                             static_cast<uint64_t>(args.dm) * 2, kPK, kPM, 128);
   if (rc == MOC_OK)
     rc = make_tmap_bf16_2d(&wmap, weight, static_cast<uint64_t>(args.dm), static_cast<uint64_t>(weight_rows),
-                           static_cast<uint64_t>(args.dm) * 2, kPK, kPNH, true);
+                           static_cast<uint64_t>(args.dm) * 2, kPK, kPNH, 128);
   if (rc != MOC_OK) return rc;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -106,6 +106,24 @@ struct TcArgs {
 __device__ __forceinline__ int lm_row(int lane) { return (lane & 7) + ((lane >> 3) & 1) * 8; }
 __device__ __forceinline__ int lm_col(int lane) { return (lane >> 4) * 8; }
 
+// Byte offset of 16-byte chunk `chunk` of alpha row `row` in a stage: the TMA box has rows of
+// ARB = 32 or 64 bytes written with the swizzle of that span, so that the 8 rows an ldmatrix
+// matrix reads fall on distinct banks (dense 32-byte rows would pair them two-way).
+template <class L>
+__device__ __forceinline__ uint32_t alpha_off(int row, int chunk) {
+  const int sw = L::ARB == 32 ? (row >> 2) & 1 : (row >> 1) & 3;
+  return static_cast<uint32_t>(row * L::ARB + ((chunk ^ sw) << 4));
+}
+
+// Float offset of column `col` of row `row` (of 16) in a warp's dalpha reduction rows: the
+// 8-float groups are permuted per row so that a warp's float2 stores to its 8 rows spread
+// over all banks (rows of 16 or 32 floats would otherwise map rows onto the same banks).
+template <int KP>
+__device__ __forceinline__ int red_off(int row, int col) {
+  const int f = KP == 16 ? ((row >> 1) & 1) : (row & 3);
+  return row * KP + (col ^ (f << 3));
+}
+
 // Shared-memory carve-up, common to both kernels.
 template <class L>
 struct Smem {
@@ -227,7 +245,6 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
   const uint32_t x_box = static_cast<uint32_t>((warp >> 2) * L::xbox);
   const int x_chunk = 2 * (warp & 3) + (lane >> 4);
   const int lrow = lm_row(lane);
-  const uint32_t a_lane = static_cast<uint32_t>(lrow * L::ARB + lm_col(lane) * 2);
   const int64_t ch_stage = ch_base + warp * 16;  // the warp's first channel
   const uint32_t ost_w = smem_addr(sm.ost + warp * 512);
 
@@ -284,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
       for (int b = 0; b < nb; ++b) {
         uint32_t af[KT][4];
 #pragma unroll
-        for (int kt = 0; kt < KT; ++kt) ldsm_x4(a_s + (16 * b) * L::ARB + kt * 32 + a_lane, af[kt]);
+        for (int kt = 0; kt < KT; ++kt) ldsm_x4(a_s + alpha_off<L>(16 * b + lrow, 2 * kt + (lane >> 4)), af[kt]);
         float acc[2][4] = {};
 #pragma unroll
         for (int s = 0; s < S; ++s) {
@@ -363,7 +380,6 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
   // swizzled x / dy boxes holding this warp's 16 channels (chunks 2*(warp&3)+{0,1})
   const uint32_t basis_base = smem_addr(basis_s);
   const int lrow = lm_row(lane);
-  const uint32_t a_lane = static_cast<uint32_t>(lrow * L::ARB + lm_col(lane) * 2);
   const uint32_t bt_lane = static_cast<uint32_t>(lrow * kRowB + (ch_w + lm_col(lane)) * 2);
   const uint32_t bn_lane =
       static_cast<uint32_t>(((lane & 7) + (lane >> 4) * 8) * kRowB + (ch_w + ((lane >> 3) & 1) * 8) * 2);
@@ -465,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt) {
         uint32_t af[4];
-        ldsm_x4(a_s + ar * L::ARB + kt * 32 + a_lane, af);
+        ldsm_x4(a_s + alpha_off<L>(ar + lrow, 2 * kt + (lane >> 4)), af);
         uint32_t b0, b1, b2, b3;
         if constexpr (BREG) {
           b0 = bw[s][kt][0], b1 = bw[s][kt][1], b2 = bw[s][kt][2], b3 = bw[s][kt][3];
@@ -529,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       uint32_t ab[DB ? KT : 1][4];  // alpha as the B operand of dbasis (tokens x bases)
       if constexpr (DB) {
 #pragma unroll
-        for (int kt = 0; kt < KT; ++kt) ldsm_x4_t(a_s + (16 * b) * L::ARB + kt * 32 + a_lane, ab[kt]);
+        for (int kt = 0; kt < KT; ++kt) ldsm_x4_t(a_s + alpha_off<L>(16 * b + lrow, 2 * kt + (lane >> 4)), ab[kt]);
       }
       uint32_t dyu[4];  // dz (= dy without SiLU) of this block, packed bf16 pairs
       ldsm_x4(dy_addr(16 * b), dyu);
@@ -598,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       for (int kn = 0; kn < 2 * KT; ++kn)
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          *reinterpret_cast<float2*>(red + (g + 8 * h) * KP + kn * 8 + 2 * q) =
+          *reinterpret_cast<float2*>(red + red_off<KP>(g + 8 * h, kn * 8 + 2 * q)) =
               make_float2(daa[kn][2 * h], daa[kn][2 * h + 1]);
       if (b % L::RB == L::RB - 1 || b == nb - 1) {
         __syncthreads();
@@ -607,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
         for (int o = threadIdx.x; o < n_out; o += kThreads) {
           const int blk = o / (16 * KP), rem = o - blk * 16 * KP;
           const int row = rem / KP, k = rem - row * KP;
-          const float* rb = red_s + blk * 8 * 16 * KP + rem;
+          const float* rb = red_s + blk * 8 * 16 * KP + red_off<KP>(row, k);
           float sum = 0.f;
 #pragma unroll
           for (int w = 0; w < 8; ++w) sum += rb[w * 16 * KP];
@@ -707,11 +723,11 @@ struct Maps {
 template <class L, bool BWD>
 int make_maps(const moc_problem& p, const void* x, const void* dy, const void* alpha, Maps& m) {
   const uint64_t D = static_cast<uint64_t>(p.dim), N = static_cast<uint64_t>(p.n_tokens);
-  int rc = make_tmap_bf16_2d(&m.x, x, D, N, D * 2, 64, L::XR, true);
-  if (rc == MOC_OK && BWD) rc = make_tmap_bf16_2d(&m.dy, dy, D, N, D * 2, 64, L::FR, true);
-  if (rc == MOC_OK)
+  int rc = make_tmap_bf16_2d(&m.x, x, D, N, D * 2, 64, L::XR, 128);
+  if (rc == MOC_OK && BWD) rc = make_tmap_bf16_2d(&m.dy, dy, D, N, D * 2, 64, L::FR, 128);
+  if (rc == MOC_OK)  // alpha rows of KP bases (32 or 64 bytes), swizzled over their span
     rc = make_tmap_bf16_2d(&m.a, alpha, static_cast<uint64_t>(p.n_bases), N, static_cast<uint64_t>(p.n_bases) * 2,
-                           L::KP, L::AR, false);
+                           L::KP, L::AR, L::ARB);
   return rc;
 }
 

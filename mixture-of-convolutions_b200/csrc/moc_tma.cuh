@@ -70,9 +70,11 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
 // Host: 2-D bf16 tensor map over a row-major [outer, inner] array with a row pitch of
-// `row_bytes`, box [box_outer, box_inner], 128-byte swizzle (or none: dense rows), zero
-// fill out of bounds.
+// `row_bytes`, box [box_outer, box_inner], zero fill out of bounds.  swizzle_bytes is the
+// shared-memory swizzle span: 128 (the 16-byte chunk index of a 128-byte row XOR row % 8),
+// 64 (chunk of a 64-byte row XOR (row / 2) % 4), 32 (chunk of a 32-byte row XOR (row / 4)
+// % 2), or 0 (dense rows).  The box's inner extent must not exceed the span.
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-                      uint32_t box_inner, uint32_t box_outer, bool swizzle128 = true);
+                      uint32_t box_inner, uint32_t box_outer, int swizzle_bytes = 128);
 
 }  // namespace moc
