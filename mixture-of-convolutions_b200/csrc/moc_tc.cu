@@ -75,17 +75,19 @@ struct Layout {
   static constexpr int red_bytes = (BWD && PART != kBwdDb) ? RB * 8 * 16 * KP * 4 : 0;
   // with register-resident basis fragments the basis staging area is reused for the
   // dalpha reduction buffer once the fragments are loaded
+  // the forward at 32 bases and more than 4 taps stages its basis (up to 68 KB) through the
+  // stage buffers, a few taps per pass, before the first tile is loaded: its fragments live
+  // in registers afterwards, and two CTAs then fit an SM
+  static constexpr bool BALIAS = !BWD && KT * S > 8;
   static constexpr int head_bytes =
-      align1k((BWD && BREG) ? (basis_bytes > red_bytes ? basis_bytes : red_bytes) : basis_bytes + red_bytes);
+      BALIAS ? 0
+             : align1k((BWD && BREG) ? (basis_bytes > red_bytes ? basis_bytes : red_bytes) : basis_bytes + red_bytes);
   // the SiLU backward writes dz in place of dy (bf16, same swizzled tile): no staging of its own
   static constexpr int dz_bytes = 0;
   // per-warp output staging: one 16-row x 16-channel bf16 block (32-byte rows)
   static constexpr int ost_bytes = BWD ? 0 : 8 * 16 * 32;
   static constexpr int total = 1024 + 2 * stage_bytes + head_bytes + dz_bytes + ost_bytes + 64;
-  // forward at 32 bases and more than 4 taps: its 68 KB basis staging leaves room for at
-  // most two CTAs anyway, and the 64 basis fragment registers need more than 128 per thread
-  static constexpr int min_blocks =
-      BWD ? ((BREG && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 3 : (KT * S > 8 ? 1 : 2));
+  static constexpr int min_blocks = BWD ? ((BREG && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 3 : 2);
 };
 
 struct TcArgs {
@@ -144,12 +146,15 @@ struct Smem {
   }
 };
 
+// taps [s0, s0 + ns) of the basis slice into rows (s - s0) * KP + k of basis_s
 template <class L, bool BWD>
-__device__ __forceinline__ void load_basis(const TcArgs& a, char* basis_s, int64_t ch_base, int S) {
+__device__ __forceinline__ void load_basis(const TcArgs& a, char* basis_s, int64_t ch_base, int S, int s0 = 0,
+                                           int ns = -1) {
   constexpr int KP = L::KP;
-  for (int idx = threadIdx.x; idx < S * KP * 16; idx += kThreads) {
+  if (ns < 0) ns = S;
+  for (int idx = threadIdx.x; idx < ns * KP * 16; idx += kThreads) {
     const int row = idx >> 4, chunk = idx & 15;
-    const int s = row / KP, k = row - s * KP;
+    const int s = s0 + row / KP, k = row - (s - s0) * KP;
     const int64_t ch = ch_base + chunk * 8;
     const bool ok = k < a.K && ch < a.D;
     const bf16* src = ok ? a.basis + (static_cast<int64_t>(k) * S + s) * a.D + ch : a.basis;
@@ -228,8 +233,29 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
     mbar_init(sm.bar + 8, 1);
     fence_mbar_init();
   }
-  load_basis<L, false>(a, sm.head, ch_base, S);
-  cp_async_commit();
+  uint32_t bw[S][KT][4];  // basis fragments for W = alpha . basis_s (B operand, 2 channel n-tiles)
+  if constexpr (L::BALIAS) {
+    constexpr int TPP = (2 * L::stage_bytes) / (L::KP * kRowB);  // taps per pass through the stages
+#pragma unroll
+    for (int s0 = 0; s0 < S; s0 += TPP) {
+      load_basis<L, false>(a, sm.stages_p, ch_base, S, s0, s0 + TPP < S ? TPP : S - s0);
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
+#pragma unroll
+      for (int ds = 0; ds < TPP; ++ds)
+#pragma unroll
+        for (int kt = 0; kt < KT; ++kt)
+          if (s0 + ds < S)
+            ldsm_x4_t(smem_addr(sm.stages_p + (ds * L::KP + kt * 16 + lm_row(lane)) * kRowB +
+                                (warp * 16 + lm_col(lane)) * 2),
+                      bw[s0 + ds < S ? s0 + ds : 0][kt]);
+      __syncthreads();  // the stages are reused for the next pass / the tiles
+    }
+  } else {
+    load_basis<L, false>(a, sm.head, ch_base, S);
+    cp_async_commit();
+  }
   griddep_wait();  // x and alpha may come from the kernels before this one
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -248,7 +274,6 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
   const int64_t ch_stage = ch_base + warp * 16;  // the warp's first channel
   const uint32_t ost_w = smem_addr(sm.ost + warp * 512);
 
-  uint32_t bw[S][KT][4];  // basis fragments for W = alpha . basis_s (B operand, 2 channel n-tiles)
   for (int64_t it = i0; it < i1; ++it) {
     const int cur = static_cast<int>((it - i0) & 1);
     const uint32_t parity = static_cast<uint32_t>(((it - i0) >> 1) & 1);
@@ -269,15 +294,17 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
       else
         mbar_arrive(nbar);
     }
-    if (it == i0) {
-      cp_async_wait<0>();
-      __syncthreads();
+    if constexpr (!L::BALIAS) {
+      if (it == i0) {
+        cp_async_wait<0>();
+        __syncthreads();
 #pragma unroll
-      for (int s = 0; s < S; ++s)
+        for (int s = 0; s < S; ++s)
 #pragma unroll
-        for (int kt = 0; kt < KT; ++kt)
-          ldsm_x4_t(smem_addr(sm.head + (s * L::KP + kt * 16 + lrow) * kRowB + (warp * 16 + lm_col(lane)) * 2),
-                    bw[s][kt]);
+          for (int kt = 0; kt < KT; ++kt)
+            ldsm_x4_t(smem_addr(sm.head + (s * L::KP + kt * 16 + lrow) * kRowB + (warp * 16 + lm_col(lane)) * 2),
+                      bw[s][kt]);
+      }
     }
     if (it + 1 == i1) griddep_launch_dependents();  // the CTA's last item
     int64_t ss, se, r0, r1;
