@@ -502,7 +502,7 @@ def run_proj(args, rank: int, world: int, local_rank: int) -> None:
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
     c = PROJ
-    B, T, Dm = c["B"], c["T"], c["d_model"]
+    B, T, Dm = (c["B"] if args.batch is None else args.batch), c["T"], c["d_model"]
     torch.manual_seed(1234)
     mods = []
     for name, D, ract in c["modules"]:
@@ -591,11 +591,14 @@ def run_proj(args, rank: int, world: int, local_rank: int) -> None:
 
 def bench_config(cfg: dict, world: int) -> dict:
     """The workload description both arms print."""
+    b = cfg["B"]
     if cfg["D"] == CONFIG_LARGE["D"]:
-        name = (f"config5: large data-parallel MoC fwd+bwd, B=4 per GPU (B={4 * world} over {world}), T=8192, "
+        name = (f"config5: large data-parallel MoC fwd+bwd, B={b} per GPU (B={b * world} over {world}), T=8192, "
                 "D=z_dim=4096 K=32 S=8 bf16 softmax, fan-in init")
     else:
-        name = "config2: MoC module fwd+bwd, B=4 T=4096 D=z_dim=2048 K=16 S=4 bf16 softmax"
+        name = f"config2: MoC module fwd+bwd, B={b} T=4096 D=z_dim=2048 K=16 S=4 bf16 softmax"
+    if b != (CONFIG_LARGE if cfg["D"] == CONFIG_LARGE["D"] else CONFIG)["B"]:
+        name += " (reduced batch, --batch)"
     in_mib = 3 * cfg["B"] * cfg["T"] * cfg["D"] * 2 // (1 << 20)
     return {"workload": name,
             "global_batch": cfg["B"] * world, "seq_len": cfg["T"], "D": cfg["D"], "z_dim": cfg["Dz"],
@@ -632,6 +635,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per rank for train / large / proj (a smaller case for ncu captures; "
+                         "default: the config's)")
     ap.add_argument("--workload", choices=("train", "decode", "varlen", "large", "proj"), default="train",
                     help="train: config 2 (the headline); decode: config 4, three modules, batch 128; "
                          "varlen: config 3, packed sequences, exp router, SiLU; large: config 5, "
@@ -664,6 +670,8 @@ def main() -> None:
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
     cfg = dict(CONFIG_LARGE if args.workload == "large" else CONFIG)
+    if args.batch is not None:
+        cfg["B"] = args.batch
     N_rank = cfg["B"] * cfg["T"]
 
     m, host = make_module_and_inputs(cfg, rank, device)
