@@ -110,7 +110,9 @@ __device__ __forceinline__ int lm_col(int lane) { return (lane >> 4) * 8; }
 
 // Byte offset of 16-byte chunk `chunk` of alpha row `row` in a stage: the TMA box has rows of
 // ARB = 32 or 64 bytes written with the swizzle of that span, so that the 8 rows an ldmatrix
-// matrix reads fall on distinct banks (dense 32-byte rows would pair them two-way).
+// matrix reads fall on distinct banks (dense 32-byte rows would pair them two-way).  The
+// swizzle repeats every 8 rows, so row 16 b + r is 16 b ARB bytes past row r: callers add
+// that part separately and keep this one free of the block index.
 template <class L>
 __device__ __forceinline__ uint32_t alpha_off(int row, int chunk) {
   const int sw = L::ARB == 32 ? (row >> 2) & 1 : (row >> 1) & 3;
@@ -328,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
       for (int b = 0; b < nb; ++b) {
         uint32_t af[KT][4];
 #pragma unroll
-        for (int kt = 0; kt < KT; ++kt) ldsm_x4(a_s + alpha_off<L>(16 * b + lrow, 2 * kt + (lane >> 4)), af[kt]);
+        for (int kt = 0; kt < KT; ++kt) ldsm_x4(a_s + (16 * b) * L::ARB + alpha_off<L>(lrow, 2 * kt + (lane >> 4)), af[kt]);
         float acc[2][4] = {};
 #pragma unroll
         for (int s = 0; s < S; ++s) {
@@ -508,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt) {
         uint32_t af[4];
-        ldsm_x4(a_s + alpha_off<L>(ar + lrow, 2 * kt + (lane >> 4)), af);
+        ldsm_x4(a_s + (ar & ~15) * L::ARB + alpha_off<L>((ar & 15) + lrow, 2 * kt + (lane >> 4)), af);
         uint32_t b0, b1, b2, b3;
         if constexpr (BREG) {
           b0 = bw[s][kt][0], b1 = bw[s][kt][1], b2 = bw[s][kt][2], b3 = bw[s][kt][3];
@@ -572,7 +574,8 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       uint32_t ab[DB ? KT : 1][4];  // alpha as the B operand of dbasis (tokens x bases)
       if constexpr (DB) {
 #pragma unroll
-        for (int kt = 0; kt < KT; ++kt) ldsm_x4_t(a_s + alpha_off<L>(16 * b + lrow, 2 * kt + (lane >> 4)), ab[kt]);
+        for (int kt = 0; kt < KT; ++kt)
+          ldsm_x4_t(a_s + (16 * b) * L::ARB + alpha_off<L>(lrow, 2 * kt + (lane >> 4)), ab[kt]);
       }
       uint32_t dyu[4];  // dz (= dy without SiLU) of this block, packed bf16 pairs
       ldsm_x4(dy_addr(16 * b), dyu);
