@@ -380,7 +380,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const uint32_t xs = smem_addr(x_s);
     const uint32_t x_box = static_cast<uint32_t>((e >> 2) * kPXBox);
     const int x_chunk = 2 * (e & 3) + (lane >> 4);
-    const uint32_t a_lane = static_cast<uint32_t>(lrow * kPARB + lcol * 2);
+    const uint32_t a_lane = static_cast<uint32_t>(lrow * kPARB + (((lane >> 4) ^ ((lrow >> 2) & 1)) << 4));
     const uint32_t ost_w = smem_addr(o_s + e * 512);
     uint32_t bw[S][4];  // basis fragments of this warp's 16 channels
     int li = 0;
@@ -397,7 +397,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         const int r = et >> 1, chunk = et & 1;
         const bool ok = r < c.rows && chunk * 8 < md.K;
         const bf16* src = ok ? md.alpha + (c.m0 + r) * md.K + chunk * 8 : md.alpha;
-        cp_async16(smem_addr(a_s + r * kPARB + chunk * 16), src, ok ? 16u : 0u);
+        // 32-byte rows with the 16-byte halves swapped every 4 rows: conflict-free ldmatrix
+        cp_async16(smem_addr(a_s + r * kPARB + ((chunk ^ ((r >> 2) & 1)) << 4)), src, ok ? 16u : 0u);
       }
       bool ok = true;
       for (int hh = 0; hh < halves; ++hh) {
