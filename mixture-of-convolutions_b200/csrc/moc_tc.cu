@@ -82,11 +82,10 @@ struct Layout {
   static constexpr int head_bytes =
       BALIAS ? 0
              : align1k((BWD && BREG) ? (basis_bytes > red_bytes ? basis_bytes : red_bytes) : basis_bytes + red_bytes);
-  // the SiLU backward writes dz in place of dy (bf16, same swizzled tile): no staging of its own
-  static constexpr int dz_bytes = 0;
   // per-warp output staging: one 16-row x 16-channel bf16 block (32-byte rows)
   static constexpr int ost_bytes = BWD ? 0 : 8 * 16 * 32;
-  static constexpr int total = 1024 + 2 * stage_bytes + head_bytes + dz_bytes + ost_bytes + 64;
+  // (the SiLU backward needs no staging of its own: it writes dz, bf16, over dy in the tile)
+  static constexpr int total = 1024 + 2 * stage_bytes + head_bytes + ost_bytes + 64;
   static constexpr int min_blocks = BWD ? ((BREG && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 3 : 2);
 };
 
@@ -134,7 +133,6 @@ struct Smem {
   uint32_t stages;  // 2 stages, 1024-byte aligned
   char* stages_p;
   char* head;       // basis staging / dalpha reduction
-  char* dz;         // fp32 dz (SiLU backward)
   char* ost;        // per-warp output staging
   uint32_t bar;     // 2 mbarriers
   __device__ explicit Smem(char* raw) {
@@ -142,8 +140,7 @@ struct Smem {
     stages_p = base;
     stages = smem_addr(base);
     head = base + 2 * L::stage_bytes;
-    dz = head + L::head_bytes;
-    ost = dz + L::dz_bytes;
+    ost = head + L::head_bytes;
     bar = smem_addr(ost + L::ost_bytes);
   }
 };
