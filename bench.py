@@ -300,7 +300,7 @@ def run_decode(args, rank: int, world: int, local_rank: int) -> None:
         xs = [h.to(device) for h in host_x]
         z = host_z.to(device)
 
-        def step():  # one fused decode step: two launches for all modules
+        def step():  # one fused decode step: one launch for all modules
             return decode_step(mods, xs, z, caches)
 
         def step_per_module():  # MoC.step per module: router + update, six launches

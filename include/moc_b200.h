@@ -92,10 +92,11 @@ const char* moc_last_cuda_error(void);
  * streams); lets a caller count launches over a region of work. */
 uint64_t moc_launch_count(void);
 
-/* Device status word of the TMA-staged kernels, OR of MOC_STATUS_* bits recorded since
- * the last clear (synchronous: reads device memory).  A staging wait that runs out of
- * its poll budget records MOC_STATUS_WAIT_TIMEOUT and the kernel returns without
- * writing its outputs instead of hanging. */
+/* Device status word of the TMA-staged kernels and of the fused decode step, OR of
+ * MOC_STATUS_* bits recorded since the last clear (synchronous: reads device memory).  A
+ * staging wait, or a wait of the decode step for another CTA's data, that runs out of its
+ * poll budget records MOC_STATUS_WAIT_TIMEOUT and the kernel returns without writing its
+ * outputs instead of hanging. */
 #define MOC_STATUS_WAIT_TIMEOUT 1
 int moc_device_status(int* status, int clear);
 
@@ -216,14 +217,14 @@ typedef struct moc_decode_module {
 #define MOC_DECODE_MAX_MODULES 4
 
 /* Fused decode step of up to MOC_DECODE_MAX_MODULES modules that share z [batch, z_dim]:
- * one launch computes every module's router (z read once per token tile), a second
- * launch mixes and convolves every module's channels and shifts its cache.  Results
+ * one launch computes every module's router and, in the same clusters of CTAs, mixes
+ * and convolves every module's channels and shifts its cache.  Results
  * agree with moc_router_forward followed by moc_step for each module within the bf16
  * tolerance: here the alpha.basis products enter an fp32 tensor-core sum exactly, where
  * moc_step (like the reference's decode kernel) rounds each product to bf16.  All modules share
  * one kernel_size; dim and z_dim must be multiples of 8 and every pointer 16-byte aligned.  Replaces, per module, the router
  * lines of MoC.forward (moc/api.py:383-388) and launch_update (moc/ops.py:341-362) with
- * two launches for all modules (the fused multi-module decode of the reference's
+ * one launch for all modules (the fused multi-module decode of the reference's
  * q / k / v usage, README.md:120-129). */
 int moc_decode_step_multi(int32_t n_modules, const moc_decode_module* modules, int64_t batch,
                           int64_t z_dim, const void* z, void* stream);

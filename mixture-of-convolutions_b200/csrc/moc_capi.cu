@@ -126,13 +126,14 @@ uint64_t moc_launch_count(void) { return g_launches.load(std::memory_order_relax
 
 int moc_device_status(int* status, int clear) {
   if (status == nullptr) return MOC_ERR_INVALID_ARGUMENT;
-  int r = 0, c = 0, m = 0, j = 0;
+  int r = 0, c = 0, m = 0, j = 0, d = 0;
   int rc = router_status(&r, clear != 0);
   if (rc == MOC_OK) rc = conv_status(&c, clear != 0);
   if (rc == MOC_OK) rc = comm_status(&m, clear != 0);
   if (rc == MOC_OK) rc = proj_status(&j, clear != 0);
+  if (rc == MOC_OK) rc = decode_status(&d, clear != 0);
   if (rc != MOC_OK) return rc;
-  *status = r | c | m | j;
+  *status = r | c | m | j | d;
   return MOC_OK;
 }
 

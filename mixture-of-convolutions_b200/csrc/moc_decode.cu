@@ -1,59 +1,63 @@
 // Fused decode step for several MoC modules that share the routing input z (the q / k / v
 // convolutions of an attention block, reference README.md:120-129), bf16.
 //
-// Two launches for all modules instead of a router GEMM, an activation and an update
-// kernel per module:
-//   k_dec_router  a cluster of 8 CTAs per (16 tokens, module).  CTA r of the cluster
-//                 streams z and the module's router weight for the 512-column chunks
-//                 r, r+8, ... through a 2-stage cp.async ring; its 8 warps own 64 columns
-//                 of a chunk each and accumulate the 16 x 16 logit tile with mma.sync
-//                 (bf16 -> fp32).  The partial tiles are added in shared memory, every CTA
-//                 stores its tile into CTA 0's shared memory (distributed shared memory),
-//                 and CTA 0 adds the 8 tiles in rank order and applies softmax / exp per
-//                 token over 16 lanes (moc/api.py:383-388).
-//   k_dec_update  CTA = (128 channels of one module, 16 tokens), launched as a programmatic
-//                 dependent of the router: the basis slice, x and cache tiles arrive with
-//                 16-byte copies while the router still runs, alpha once it has finished; per tap, one ldmatrix of
-//                 the basis and two mma.sync per warp form W_s = alpha . basis_s for 16
-//                 tokens x 16 channels (bf16 products exact, fp32 sums: the rounding of the
-//                 reference's bf16 forward, moc/kernels.py:125-130; its decode kernel rounds
-//                 each product to bf16 first, moc/kernels.py:466-513, a difference far inside
-//                 the bf16 tolerance).  Then y = [silu](sum_s state_s * W_s), the cache rows
-//                 are shifted in shared memory with x appended (moc/kernels.py:522-550),
-//                 and y and the cache tile leave with 16-byte stores.
+// One launch for all modules instead of a router GEMM, an activation and an update kernel
+// per module.  k_dec_step runs as clusters of 8 CTAs; a cluster covers 16 tokens and up to
+// 8 x 128 channels of one module (a module wider than 1024 channels takes several
+// clusters, each of which routes the 16 tokens itself).  Each CTA:
+//   1. starts the 16-byte copies of its update tiles (the basis slice of its 128 channels,
+//      x and the cache rows of its 16 tokens), none of which depend on the router;
+//   2. computes its share of the 16 x K router logits: warp w of CTA r owns the 32-column
+//      groups r*8 + w, r*8 + w + 64, ... of z_dim and reads them straight from global memory
+//      into mma.sync fragments (bf16 -> fp32), with no shared-memory staging;
+//   3. adds its warps' tiles in shared memory and stores the sum into CTA 0's shared memory
+//      (distributed shared memory); CTA 0 adds the 8 tiles in rank order, applies softmax /
+//      exp per token over 16 lanes (moc/api.py:383-388), writes alpha and stores its bf16
+//      value into the alpha tile of every CTA of the cluster;
+//   4. per tap, one ldmatrix of the basis and two mma.sync per warp form W_s = alpha . basis_s
+//      for 16 tokens x 16 channels (bf16 products exact, fp32 sums: the rounding of the
+//      reference's bf16 forward, moc/kernels.py:125-130; its decode kernel rounds each
+//      product to bf16 first, moc/kernels.py:466-513, a difference far inside the bf16
+//      tolerance).  The epilogue works on the MMA's output fragments: each thread owns
+//      (token, channel pair) positions, reads the state there, forms y = [silu](sum_s
+//      state_s * W_s), shifts the pair's cache rows with x appended (moc/kernels.py:522-550),
+//      and y and the cache tile leave with 16-byte stores.
 #include <algorithm>
+#include <climits>
 
 #include "moc_common.cuh"
 #include "moc_internal.h"
 #include "moc_mma.cuh"
+#include "moc_tma.cuh"
 
 namespace moc {
 
+// status word of the decode kernel (bounded-wait timeouts), read by moc_device_status()
+__device__ int g_dec_status;
+
 namespace {
 
-constexpr int kDecTok = 16;                  // tokens per router CTA (MMA M)
-constexpr int kDecCols = 512;                // z columns per staged chunk
-constexpr int kDecPitch = kDecCols * 2 + 16; // smem row pitch in bytes (16 B pad: conflict-free ldmatrix)
+constexpr int kDecTok = 16;                  // tokens per cluster (MMA M)
 constexpr int kDecKP = 16;                   // bases per module, padded (MMA N = 2 x 8)
-constexpr int kDecStageRows = kDecTok + kDecKP;
-constexpr int kDecStageBytes = kDecStageRows * kDecPitch;
-constexpr int kDecCluster = 8;               // CTAs per router cluster (split of z_dim)
-constexpr int kDecRouterSmem = 2 * kDecStageBytes + (8 + kDecCluster) * kDecTok * kDecKP * 4;
-constexpr int kUpdTok = 16;                  // tokens per update CTA (MMA M)
-constexpr int kUpdThreads = 256;             // 8 warps x 16 channels (two MMA n-tiles)
-constexpr int kUpdCh = 128;                  // channels per update CTA
-constexpr int kUpdBasisPitch = kUpdCh * 2 + 16;  // padded rows: conflict-free ldmatrix
-constexpr int kUpdAlphaPitch = 48;
-constexpr int kUpdWPitch = kUpdCh * 4 + 16;     // fp32 W rows, padded
+constexpr int kDecCluster = 8;               // CTAs per cluster (split of z_dim and of the channels)
+constexpr int kDecThreads = 256;             // 8 warps
+constexpr int kDecGroupCols = 32;            // z columns per router group (two MMA k-steps)
+constexpr int kDecCh = 128;                  // channels per CTA
+constexpr int kDecBasisPitch = kDecCh * 2 + 16;  // padded rows: conflict-free ldmatrix
+constexpr int kDecAlphaPitch = 48;
+constexpr int kDecXPitch = kDecCh * 2 + 16;      // x / y rows, padded: conflict-free pair reads
 
 template <int S>
-struct UpdLayout {
-  static constexpr int basis = S * kDecKP * kUpdBasisPitch;
-  static constexpr int alpha = kUpdTok * kUpdAlphaPitch;
-  static constexpr int x = kUpdTok * kUpdCh * 2;
-  static constexpr int cache = kUpdTok * kUpdCh * S * 2;
-  static constexpr int w = S * kUpdTok * kUpdWPitch;
-  static constexpr int total = basis + alpha + x + cache + w;
+struct DecLayout {
+  static constexpr int cache_pitch = kDecCh * S * 2 + 64;  // padded: two token rows per quarter-warp on distinct banks
+  static constexpr int basis = S * kDecKP * kDecBasisPitch;
+  static constexpr int alpha = kDecTok * kDecAlphaPitch;
+  static constexpr int x = kDecTok * kDecXPitch;
+  static constexpr int cache = kDecTok * cache_pitch;
+  static constexpr int red = 8 * kDecTok * kDecKP * 4;            // per-warp logit tiles
+  static constexpr int part = kDecCluster * kDecTok * kDecKP * 4;  // CTA 0: the cluster's CTA sums
+  static constexpr int bars = 16;                                  // two mbarriers
+  static constexpr int total = basis + alpha + x + cache + red + part + bars;
 };
 
 struct DecModule {
@@ -70,27 +74,24 @@ struct DecModule {
 struct DecArgs {
   DecModule m[MOC_DECODE_MAX_MODULES];
   int n_mod;
+  int n_parts;  // clusters per 16-token group, over all modules
   int64_t B, Dz;
   const bf16* z;
-  int blk_prefix[MOC_DECODE_MAX_MODULES + 1];  // update-kernel channel blocks, prefix sums over modules
+  int part_prefix[MOC_DECODE_MAX_MODULES + 1];  // clusters per token group, prefix sums over modules
 };
 
 __device__ __forceinline__ int lm_row_d(int lane) { return (lane & 7) + ((lane >> 3) & 1) * 8; }
 __device__ __forceinline__ int lm_col_d(int lane) { return (lane >> 4) * 8; }
 
-// Programmatic dependent launch: the router lets the update grid start at once; the update
-// kernel stages everything that does not depend on the router (basis, x, cache) and then
-// waits for the router grid's completion (and its alpha) before reading alpha.  Without the
-// launch attribute both are no-ops and the kernels run one after the other.
-__device__ __forceinline__ void griddep_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+// Both cluster barriers of the kernel are split into an arrive and a wait.  The first: arrive
+// at the start (after the mbarrier initialisation), wait before the first store into another
+// CTA's shared memory, so that every CTA of the cluster is running with its mbarriers ready.
+// The second: arrive after the CTA's last store into another CTA, wait just before exit, so
+// that no CTA leaves while another may still write into its shared memory.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
 }
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
-  asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -98,94 +99,181 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   return r;
 }
 
-// Stores v at shared address `addr` (this CTA's layout) of CTA `rank` of the cluster.
-__device__ __forceinline__ void st_dsmem(uint32_t addr, uint32_t rank, float v) {
+// Address of the shared-memory location `addr` (this CTA's layout) in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(addr), "r"(rank));
-  asm volatile("st.shared::cluster.f32 [%0], %1;\n" ::"r"(remote), "f"(v) : "memory");
+  return remote;
+}
+// Asynchronous 4-byte store into another CTA's shared memory; its arrival counts 4 bytes
+// on that CTA's mbarrier (`remote_bar`, mapped like `remote_addr`).
+__device__ __forceinline__ void st_async_b32(uint32_t remote_addr, uint32_t remote_bar, uint32_t v) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];\n" ::"r"(remote_addr),
+               "r"(v), "r"(remote_bar)
+               : "memory");
+}
+// Polls this CTA's mbarrier phase `parity` at most kSpinLimit times, with acquire at cluster
+// scope (the bytes it counts were written by other CTAs); true once the phase completed.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
 }
 
-__global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(256)
-    k_dec_router(const __grid_constant__ DecArgs a) {
-  extern __shared__ __align__(128) char smem[];
-  float* red = reinterpret_cast<float*>(smem + 2 * kDecStageBytes);  // [8 warps][16 tokens][16 bases]
-  float* part = red + 8 * kDecTok * kDecKP;  // [8 ranks][16 tokens][16 bases]: the cluster's CTA sums (rank 0's)
-  const DecModule& mod = a.m[blockIdx.y];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();
-  const int64_t tok0 = static_cast<int64_t>(blockIdx.x / kDecCluster) * kDecTok;
-  const int n_chunks = static_cast<int>((a.Dz + kDecCols - 1) / kDecCols);
-  griddep_launch_dependents();
+__device__ __forceinline__ uint4 ldg16_or_zero(const bf16* p, bool ok) {
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (ok) v = __ldg(reinterpret_cast<const uint4*>(p));
+  return v;
+}
 
-  auto load = [&](int c, int st) {
-    char* base = smem + st * kDecStageBytes;
-    const int64_t col0 = static_cast<int64_t>(c) * kDecCols;
-    for (int idx = threadIdx.x; idx < kDecStageRows * (kDecCols / 8); idx += 256) {
-      const int row = idx / (kDecCols / 8), piece = idx - row * (kDecCols / 8);
-      const int64_t col = col0 + piece * 8;
-      const bf16* src;
-      bool ok;
-      if (row < kDecTok) {
-        const int64_t t = tok0 + row;
-        ok = t < a.B && col < a.Dz;
-        src = a.z + t * a.Dz + col;
-      } else {
-        const int k = row - kDecTok;
-        ok = k < mod.K && col < a.Dz;
-        src = mod.w + static_cast<int64_t>(k) * a.Dz + col;
-      }
-      cp_async16(smem_addr(base + row * kDecPitch + piece * 16), ok ? src : a.z, ok ? 16u : 0u);
+template <int S>
+__global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(kDecThreads, 3)
+    k_dec_step(const __grid_constant__ DecArgs a) {
+  extern __shared__ __align__(128) char smem[];
+  using L = DecLayout<S>;
+  char* basis_s = smem;                // [tap][base][128 ch], bases past K zero
+  char* alpha_s = basis_s + L::basis;  // [token][16 bases]
+  char* x_s = alpha_s + L::alpha;      // [token][128 ch]; y replaces x in place
+  char* cache_s = x_s + L::x;          // [token][128 ch][S]
+  float* red = reinterpret_cast<float*>(cache_s + L::cache);  // [8 warps][16 tokens][16 bases]
+  float* part = red + 8 * kDecTok * kDecKP;                    // [8 ranks][16 tokens][16 bases]
+  const int cid = static_cast<int>(blockIdx.x / kDecCluster);
+  const int tg = cid / a.n_parts, cl = cid - tg * a.n_parts;  // token group, cluster within it
+  int m = 0;
+  while (m + 1 < a.n_mod && cl >= a.part_prefix[m + 1]) ++m;
+  const DecModule& mod = a.m[m];
+  const int part_idx = cl - a.part_prefix[m];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const uint32_t rank = cluster_rank();
+  const int64_t b0 = static_cast<int64_t>(tg) * kDecTok;
+  const int64_t c0 = (static_cast<int64_t>(part_idx) * kDecCluster + rank) * kDecCh;
+  const bool has_blk = c0 < mod.D;  // CTA-uniform
+  const int nch = has_blk ? static_cast<int>(mod.D - c0 < kDecCh ? mod.D - c0 : kDecCh) : 0;  // multiple of 8
+  const int ntok = static_cast<int>(a.B - b0 < kDecTok ? a.B - b0 : kDecTok);
+  const uint32_t bar_part = smem_addr(reinterpret_cast<char*>(part) + L::part);  // CTA 0: the other CTAs' tiles
+  const uint32_t bar_alpha = bar_part + 8;                                         // CTAs 1..7: the alpha tile
+  if (threadIdx.x == 0) {
+    mbar_init(bar_part, 1);
+    mbar_init(bar_alpha, 1);
+    if (rank == 0)
+      mbar_expect_tx(bar_part, (kDecCluster - 1) * kDecTok * kDecKP * 4);
+    else
+      mbar_expect_tx(bar_alpha, kDecTok * kDecKP * 2);
+    fence_mbar_init();
+  }
+  cluster_arrive_relaxed();
+
+  // ---- 1. router loads of the first pair of column groups, then the copies of the update
+  // tiles, which are not needed before the router has finished.
+  // Router: lane (g, q) reads columns 8q..8q+7 of a 32-column group for tokens g, g+8 and
+  // bases g, g+8 (one 16-byte load each); the MMA k-slots 2q, 2q+1, 2q+8, 2q+9 of the first
+  // k-step take columns 8q..8q+3, those of the second 8q+4..8q+7 (A and B use the same
+  // order, and a dot product does not depend on it).  Warp w of CTA r owns the groups
+  // r*8 + w, r*8 + w + 64, ...
+  const int n_groups = static_cast<int>((a.Dz + kDecGroupCols - 1) / kDecGroupCols);
+  const bool ok_lo = b0 + g < a.B, ok_hi = b0 + g + 8 < a.B;
+  const bool ok_w0 = g < mod.K, ok_w1 = g + 8 < mod.K;
+  const bf16* z_lo = a.z + (ok_lo ? b0 + g : 0) * a.Dz;
+  const bf16* z_hi = a.z + (ok_hi ? b0 + g + 8 : 0) * a.Dz;
+  const bf16* w0 = mod.w + static_cast<int64_t>(ok_w0 ? g : 0) * a.Dz;
+  const bf16* w1 = mod.w + static_cast<int64_t>(ok_w1 ? g + 8 : 0) * a.Dz;
+  constexpr int kStride = kDecCluster * 8;  // groups per sweep of the cluster's 64 warps
+  uint4 v[2][4];  // [group of the pair][z token g, z token g+8, w base g, w base g+8]
+  auto load_pair = [&](int gi) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int gu = gi + u * kStride;
+      const int64_t col = static_cast<int64_t>(gu) * kDecGroupCols + 8 * q;
+      const bool okc = gu < n_groups && col < a.Dz;  // z_dim is a multiple of 8
+      v[u][0] = ldg16_or_zero(z_lo + col, okc && ok_lo);
+      v[u][1] = ldg16_or_zero(z_hi + col, okc && ok_hi);
+      v[u][2] = ldg16_or_zero(w0 + col, okc && ok_w0);
+      v[u][3] = ldg16_or_zero(w1 + col, okc && ok_w1);
     }
   };
+  int gi = static_cast<int>(rank) * 8 + warp;
+  load_pair(gi);
 
-  // this CTA's chunks: rank, rank + 8, ...
-  float acc[2][4] = {};
-  int n = 0;
-  if (static_cast<int>(rank) < n_chunks) {
-    load(rank, 0);
+  // update tiles (16-byte pieces; missing channels, tokens and bases become zeros)
+  constexpr int kPieces = kDecCh / 8;  // 16-byte pieces per 128-channel row
+  if (has_blk) {
+    for (int i = threadIdx.x; i < S * kDecKP * kPieces; i += kDecThreads) {
+      const int row = i / kPieces, p = i - row * kPieces;  // row = s * 16 + k
+      const int s = row / kDecKP, k = row - s * kDecKP;
+      const bool ok = k < mod.K && p * 8 < nch;
+      cp_async16(smem_addr(basis_s + row * kDecBasisPitch + p * 16),
+                 ok ? mod.basis + (static_cast<int64_t>(k) * S + s) * mod.D + c0 + p * 8 : mod.basis,
+                 ok ? 16u : 0u);
+    }
+    for (int i = threadIdx.x; i < kDecTok * kPieces; i += kDecThreads) {
+      const int t = i / kPieces, p = i - t * kPieces;
+      const bool ok = t < ntok && p * 8 < nch;
+      cp_async16(smem_addr(x_s + t * kDecXPitch + p * 16), ok ? mod.x + (b0 + t) * mod.D + c0 + p * 8 : mod.x,
+                 ok ? 16u : 0u);
+    }
+    for (int i = threadIdx.x; i < kDecTok * kPieces * S; i += kDecThreads) {
+      const int t = i / (kPieces * S), p = i - t * kPieces * S;  // 16-byte piece p of the token's row
+      const bool ok = t < ntok && p * 8 < nch * S;
+      cp_async16(smem_addr(cache_s + t * L::cache_pitch + p * 16),
+                 ok ? mod.cache + ((b0 + t) * mod.D + c0) * S + p * 8 : mod.cache, ok ? 16u : 0u);
+    }
     cp_async_commit();
   }
-  for (int c = rank; c < n_chunks; c += kDecCluster, ++n) {
-    if (c + kDecCluster < n_chunks) {
-      load(c + kDecCluster, (n + 1) & 1);  // the stage of this CTA's previous chunk, released below
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const uint32_t zs = smem_addr(smem + (n & 1) * kDecStageBytes);
-    const uint32_t ws = zs + kDecTok * kDecPitch;
+
+  // ---- 2. router logits of this CTA's column groups
+  float acc[2][4] = {};
+#pragma unroll 1
+  for (;;) {
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const int col = warp * 64 + kk * 16;
-      uint32_t af[4], bf[4];
-      ldsm_x4(zs + lm_row_d(lane) * kDecPitch + (col + lm_col_d(lane)) * 2, af);
-      ldsm_x4(ws + ((lane & 7) + (lane >> 4) * 8) * kDecPitch + (col + ((lane >> 3) & 1) * 8) * 2, bf);
-      mma_bf16(acc[0], af, bf[0], bf[1]);
-      mma_bf16(acc[1], af, bf[2], bf[3]);
+    for (int u = 0; u < 2; ++u) {
+      const uint32_t a_lo[4] = {v[u][0].x, v[u][1].x, v[u][0].y, v[u][1].y};
+      const uint32_t a_hi[4] = {v[u][0].z, v[u][1].z, v[u][0].w, v[u][1].w};
+      mma_bf16(acc[0], a_lo, v[u][2].x, v[u][2].y);
+      mma_bf16(acc[1], a_lo, v[u][3].x, v[u][3].y);
+      mma_bf16(acc[0], a_hi, v[u][2].z, v[u][2].w);
+      mma_bf16(acc[1], a_hi, v[u][3].z, v[u][3].w);
     }
-    __syncthreads();
+    gi += 2 * kStride;
+    if (gi >= n_groups) break;
+    load_pair(gi);
   }
 
+  // ---- 3. reduction: warps in shared memory, CTAs in CTA 0's shared memory, in rank order.
   // acc[nt][2h + e] = partial logit (token g + 8h, base 8nt + 2q + e) of this warp's columns
-  const int g = lane >> 2, q = lane & 3;
-  float* r = red + warp * kDecTok * kDecKP;
+  {
+    float* r = red + warp * kDecTok * kDecKP;
 #pragma unroll
-  for (int nt = 0; nt < 2; ++nt)
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
-      *reinterpret_cast<float2*>(r + (g + 8 * h) * kDecKP + nt * 8 + 2 * q) =
-          make_float2(acc[nt][2 * h], acc[nt][2 * h + 1]);
+      for (int h = 0; h < 2; ++h)
+        *reinterpret_cast<float2*>(r + (g + 8 * h) * kDecKP + nt * 8 + 2 * q) =
+            make_float2(acc[nt][2 * h], acc[nt][2 * h + 1]);
+  }
   __syncthreads();
   const int t = threadIdx.x >> 4, k = threadIdx.x & 15;  // 16 lanes per token
   float l = 0.f;
 #pragma unroll
   for (int w = 0; w < 8; ++w) l += red[w * kDecTok * kDecKP + t * kDecKP + k];
-  // every CTA puts its tile into rank 0's shared memory; rank 0 adds them in rank order
-  st_dsmem(smem_addr(part + (rank * kDecTok + t) * kDecKP + k), 0, l);
-  cluster_sync_all();
-  if (rank == 0) {
+  const uint32_t part_off = smem_addr(part + (rank * kDecTok + t) * kDecKP + k);
+  cluster_wait();  // every CTA of the cluster is running, its mbarriers initialised
+  bool timed_out;
+  if (rank != 0) {
+    st_async_b32(map_rank(part_off, 0), map_rank(bar_part, 0), __float_as_uint(l));
+    cluster_arrive_relaxed();  // this CTA's last store into another CTA
+    timed_out = !mbar_wait_cluster(bar_alpha, 0);
+  } else {
+    part[t * kDecKP + k] = l;
+    timed_out = !mbar_wait_cluster(bar_part, 0);
+    __syncthreads();  // this CTA's own tile, written above
     l = 0.f;
 #pragma unroll
     for (int rr = 0; rr < kDecCluster; ++rr) l += part[(rr * kDecTok + t) * kDecKP + k];
@@ -202,168 +290,122 @@ __global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(256)
     } else {
       v = expf(l);
     }
-    const int64_t tok = tok0 + t;
-    if (tok < a.B && k < mod.K) mod.alpha[tok * mod.K + k] = __float2bfloat16_rn(v);
-  }
-}
-
-template <int S>
-__global__ void __launch_bounds__(kUpdThreads) k_dec_update(const __grid_constant__ DecArgs a) {
-  // tiles of this CTA's 16 tokens x 128 channels, loaded with 16-byte copies (dynamic
-  // shared memory, UpdLayout<S>)
-  extern __shared__ __align__(16) char upd_smem[];
-  using UL = UpdLayout<S>;
-  char* basis_s = upd_smem;                // [tap][base][128 ch], bases past K zero
-  char* alpha_s = basis_s + UL::basis;     // [token][16 bases]
-  char* x_s = alpha_s + UL::alpha;         // [token][128 ch]; y replaces x in place
-  char* cache_s = x_s + UL::x;             // [token][128 ch][S]
-  char* w_s = cache_s + UL::cache;         // [tap][token][128 ch] fp32
-  char* y_s = x_s;
-  int m = 0;
-  while (m + 1 < a.n_mod && static_cast<int>(blockIdx.x) >= a.blk_prefix[m + 1]) ++m;
-  const DecModule& mod = a.m[m];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, q = lane & 3;
-  const int64_t c0 = static_cast<int64_t>(static_cast<int>(blockIdx.x) - a.blk_prefix[m]) * kUpdCh;
-  const int64_t b0 = static_cast<int64_t>(blockIdx.y) * kUpdTok;
-  const int nch = static_cast<int>(mod.D - c0 < kUpdCh ? mod.D - c0 : kUpdCh);  // multiple of 8
-  const int ntok = static_cast<int>(a.B - b0 < kUpdTok ? a.B - b0 : kUpdTok);
-
-  // ---- loads (16-byte pieces; missing channels, tokens and bases become zeros)
-  constexpr int kPieces = kUpdCh / 8;  // 16-byte pieces per 64-channel row
-  for (int i = threadIdx.x; i < S * kDecKP * kPieces; i += kUpdThreads) {
-    const int row = i / kPieces, p = i - row * kPieces;  // row = s * 16 + k
-    const int s = row / kDecKP, k = row - s * kDecKP;
-    const bool ok = k < mod.K && p * 8 < nch;
-    cp_async16(smem_addr(basis_s + row * kUpdBasisPitch + p * 16),
-               ok ? mod.basis + (static_cast<int64_t>(k) * S + s) * mod.D + c0 + p * 8 : mod.basis, ok ? 16u : 0u);
-  }
-  for (int i = threadIdx.x; i < kUpdTok * kPieces; i += kUpdThreads) {
-    const int t = i / kPieces, p = i - t * kPieces;
-    const bool ok = t < ntok && p * 8 < nch;
-    cp_async16(smem_addr(x_s + t * kUpdCh * 2 + p * 16), ok ? mod.x + (b0 + t) * mod.D + c0 + p * 8 : mod.x,
-               ok ? 16u : 0u);
-  }
-  for (int i = threadIdx.x; i < kUpdTok * kPieces * S; i += kUpdThreads) {
-    const int t = i / (kPieces * S), p = i - t * kPieces * S;  // 16-byte piece p of the token's row
-    const bool ok = t < ntok && p * 8 < nch * S;
-    cp_async16(smem_addr(cache_s + t * kUpdCh * S * 2 + p * 16),
-               ok ? mod.cache + ((b0 + t) * mod.D + c0) * S + p * 8 : mod.cache, ok ? 16u : 0u);
-  }
-  cp_async_commit();
-  griddep_wait();  // alpha comes from the router grid
-  for (int i = threadIdx.x; i < kUpdTok * kDecKP; i += kUpdThreads) {
-    const int t = i / kDecKP, k = i - t * kDecKP;
-    const bool ok = t < ntok && k < mod.K;
-    reinterpret_cast<bf16*>(alpha_s + t * kUpdAlphaPitch)[k] = ok ? mod.alpha[(b0 + t) * mod.K + k] : bf16(0.f);
-  }
-  cp_async_wait<0>();
-  __syncthreads();
-
-  // ---- W_s = alpha . basis_s for the warp's 16 channels (two 8-channel n-tiles) and the
-  // CTA's 16 tokens, into w_s [tap][token][64 channels] fp32
-  uint32_t af[4];
-  ldsm_x4(smem_addr(alpha_s) + lm_row_d(lane) * kUpdAlphaPitch + lm_col_d(lane) * 2, af);
-  const int cw = warp * 16;
+    const bool ok = t < ntok && k < mod.K;  // padding tokens and bases get alpha 0
+    const bf16 vb = __float2bfloat16_rn(ok ? v : 0.f);
+    const uint32_t bits = __bfloat16_as_ushort(vb);
+    const uint32_t hi = __shfl_down_sync(0xffffffffu, bits, 1);  // base k + 1 of the same token
+    if ((k & 1) == 0) {  // one 4-byte store per base pair
+      const uint32_t pair = bits | (hi << 16);
+      const uint32_t off = smem_addr(alpha_s + t * kDecAlphaPitch + k * 2);
+      *reinterpret_cast<uint32_t*>(alpha_s + t * kDecAlphaPitch + k * 2) = pair;
 #pragma unroll
-  for (int s = 0; s < S; ++s) {
-    uint32_t bf[4];
-    ldsm_x4_t(smem_addr(basis_s) + (s * kDecKP + lm_row_d(lane)) * kUpdBasisPitch + (cw + lm_col_d(lane)) * 2, bf);
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      float w[4];
-      mma_bf16_z(w, af, bf[2 * nt], bf[2 * nt + 1]);  // w[2h + e]: token g + 8h, channel cw + 8nt + 2q + e
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-        *reinterpret_cast<float2*>(w_s + (s * kUpdTok + g + 8 * h) * kUpdWPitch + (cw + 8 * nt + 2 * q) * 4) =
-            make_float2(w[2 * h], w[2 * h + 1]);
+      for (int rr = 1; rr < kDecCluster; ++rr) st_async_b32(map_rank(off, rr), map_rank(bar_alpha, rr), pair);
     }
+    cluster_arrive_relaxed();  // this CTA's last store into another CTA
+    if (ok && part_idx == 0) mod.alpha[(b0 + t) * mod.K + k] = vb;
   }
-  __syncthreads();
+  timed_out = __syncthreads_or(timed_out);  // also: CTA 0's alpha tile is complete
+  if (timed_out) {
+    if (threadIdx.x == 0) atomicOr(&g_dec_status, kStatusWaitTimeout);
+    mbar_wait_cluster(rank == 0 ? bar_part : bar_alpha, 0);  // once more, bounded: stores still on the way
+  }
 
-  // ---- thread = (token, channel pair): y = [silu](sum_s state_s * W_s) with state_s = cache
-  // slot s+1, x for the newest tap; the pair's two cache rows shift in place, x appended
+  // ---- 4. update
+  cp_async_wait<0>();
+  if (has_blk && !timed_out) {
+    __syncthreads();
+    uint32_t af[4];
+    ldsm_x4(smem_addr(alpha_s) + lm_row_d(lane) * kDecAlphaPitch + lm_col_d(lane) * 2, af);
+    const int cw = warp * 16;
+    // this thread's outputs: tokens g + 8h, channels cw + 8nt + 2q + e (the MMA's C fragment)
+    uint32_t cr[2][2][S];  // [h][nt]: cache rows of the channel pair, S slots each, 2*S bf16
+    uint32_t xp[2][2];
 #pragma unroll
-  for (int it = 0; it < kUpdTok * (kUpdCh / 2) / kUpdThreads; ++it) {
-    const int item = it * kUpdThreads + threadIdx.x;
-    const int t = item / (kUpdCh / 2), ch = 2 * (item - t * (kUpdCh / 2));
-    const uint32_t xp = *reinterpret_cast<const uint32_t*>(x_s + (t * kUpdCh + ch) * 2);
-    uint32_t cr[S];  // rows of channels ch, ch+1: S slots each, 2*S bf16
-    char* crow = cache_s + (t * kUpdCh + ch) * S * 2;
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-    for (int i = 0; i < S; ++i) cr[i] = reinterpret_cast<const uint32_t*>(crow)[i];
-    auto slot = [&](int e, int i) -> uint32_t {  // channel ch+e, slot i
+      for (int nt = 0; nt < 2; ++nt) {
+        const int tt = g + 8 * h, c = cw + 8 * nt + 2 * q;
+        const uint32_t* row = reinterpret_cast<const uint32_t*>(cache_s + tt * L::cache_pitch + c * S * 2);
+#pragma unroll
+        for (int i = 0; i < S; ++i) cr[h][nt][i] = row[i];
+        xp[h][nt] = *reinterpret_cast<const uint32_t*>(x_s + tt * kDecXPitch + c * 2);
+      }
+    auto slot = [&](int h, int nt, int e, int i) -> uint32_t {  // channel c+e, slot i
       const int el = e * S + i;
-      return (cr[el >> 1] >> (16 * (el & 1))) & 0xffffu;
+      return (cr[h][nt][el >> 1] >> (16 * (el & 1))) & 0xffffu;
     };
-    float acc0 = 0.f, acc1 = 0.f;
+    float y[2][4] = {};  // [nt][2h + e]
 #pragma unroll
     for (int s = 0; s < S; ++s) {
-      const float2 w = *reinterpret_cast<const float2*>(w_s + (s * kUpdTok + t) * kUpdWPitch + ch * 4);
-      const uint32_t s0 = s == S - 1 ? (xp & 0xffffu) : slot(0, s + 1);
-      const uint32_t s1 = s == S - 1 ? (xp >> 16) : slot(1, s + 1);
-      acc0 = fmaf(__uint_as_float(s0 << 16), w.x, acc0);
-      acc1 = fmaf(__uint_as_float(s1 << 16), w.y, acc1);
-    }
-    if (mod.act) {
-      acc0 = silu_f(acc0);
-      acc1 = silu_f(acc1);
-    }
-    *reinterpret_cast<uint32_t*>(y_s + (t * kUpdCh + ch) * 2) = pack_bf16(acc0, acc1);
-    uint32_t nr[S];
+      uint32_t bf[4];
+      ldsm_x4_t(smem_addr(basis_s) + (s * kDecKP + lm_row_d(lane)) * kDecBasisPitch + (cw + lm_col_d(lane)) * 2, bf);
 #pragma unroll
-    for (int i = 0; i < S; ++i) {
-      uint32_t half[2];
+      for (int nt = 0; nt < 2; ++nt) {
+        float w[4];
+        mma_bf16_z(w, af, bf[2 * nt], bf[2 * nt + 1]);  // w[2h + e]: token g + 8h, channel cw + 8nt + 2q + e
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int el = 2 * i + j, e = el / S, sl = el - e * S;
-        half[j] = sl == S - 1 ? (e == 0 ? (xp & 0xffffu) : (xp >> 16)) : slot(e, sl + 1);
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            // state_s = cache slot s+1; x for the newest tap
+            const uint32_t st = s == S - 1 ? ((xp[h][nt] >> (16 * e)) & 0xffffu) : slot(h, nt, e, s + 1);
+            y[nt][2 * h + e] = fmaf(__uint_as_float(st << 16), w[2 * h + e], y[nt][2 * h + e]);
+          }
       }
-      nr[i] = half[0] | (half[1] << 16);
     }
 #pragma unroll
-    for (int i = 0; i < S; ++i) reinterpret_cast<uint32_t*>(crow)[i] = nr[i];
-  }
-  __syncthreads();
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int tt = g + 8 * h, c = cw + 8 * nt + 2 * q;
+        float y0 = y[nt][2 * h], y1 = y[nt][2 * h + 1];
+        if (mod.act) {
+          y0 = silu_f(y0);
+          y1 = silu_f(y1);
+        }
+        *reinterpret_cast<uint32_t*>(x_s + tt * kDecXPitch + c * 2) = pack_bf16(y0, y1);
+        uint32_t* row = reinterpret_cast<uint32_t*>(cache_s + tt * L::cache_pitch + c * S * 2);
+#pragma unroll
+        for (int i = 0; i < S; ++i) {
+          uint32_t half[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int el = 2 * i + j, e = el / S, sl = el - e * S;
+            half[j] = sl == S - 1 ? ((xp[h][nt] >> (16 * e)) & 0xffffu) : slot(h, nt, e, sl + 1);
+          }
+          row[i] = half[0] | (half[1] << 16);
+        }
+      }
+    __syncthreads();
 
-  // ---- stores (16-byte pieces)
-  for (int i = threadIdx.x; i < kUpdTok * kPieces; i += kUpdThreads) {
-    const int t = i / kPieces, p = i - t * kPieces;
-    if (t < ntok && p * 8 < nch)
-      *reinterpret_cast<uint4*>(mod.out + (b0 + t) * mod.D + c0 + p * 8) =
-          *reinterpret_cast<const uint4*>(y_s + t * kUpdCh * 2 + p * 16);
+    // ---- stores (16-byte pieces)
+    for (int i = threadIdx.x; i < kDecTok * kPieces; i += kDecThreads) {
+      const int tt = i / kPieces, p = i - tt * kPieces;
+      if (tt < ntok && p * 8 < nch)
+        *reinterpret_cast<uint4*>(mod.out + (b0 + tt) * mod.D + c0 + p * 8) =
+            *reinterpret_cast<const uint4*>(x_s + tt * kDecXPitch + p * 16);
+    }
+    for (int i = threadIdx.x; i < kDecTok * kPieces * S; i += kDecThreads) {
+      const int tt = i / (kPieces * S), p = i - tt * kPieces * S;
+      if (tt < ntok && p * 8 < nch * S)
+        *reinterpret_cast<uint4*>(mod.cache + ((b0 + tt) * mod.D + c0) * S + p * 8) =
+            *reinterpret_cast<const uint4*>(cache_s + tt * L::cache_pitch + p * 16);
+    }
   }
-  for (int i = threadIdx.x; i < kUpdTok * kPieces * S; i += kUpdThreads) {
-    const int t = i / (kPieces * S), p = i - t * kPieces * S;
-    if (t < ntok && p * 8 < nch * S)
-      *reinterpret_cast<uint4*>(mod.cache + ((b0 + t) * mod.D + c0) * S + p * 8) =
-          *reinterpret_cast<const uint4*>(cache_s + t * kUpdCh * S * 2 + p * 16);
-  }
+  cluster_wait();  // no CTA of the cluster still stores into this one
 }
 
-int g_dec_sm_configured[64];
-
 template <int S>
-cudaError_t launch_update(dim3 grid, const DecArgs& a, cudaStream_t st, int dev) {
+cudaError_t launch_step(unsigned grid, const DecArgs& a, cudaStream_t st, int dev) {
   static bool configured[64] = {};
   if (dev < 0 || dev >= 64 || !configured[dev]) {
     const cudaError_t e =
-        cudaFuncSetAttribute(k_dec_update<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, UpdLayout<S>::total);
+        cudaFuncSetAttribute(k_dec_step<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecLayout<S>::total);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  // launched as a programmatic dependent of the router (its loads overlap the router)
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kUpdThreads);
-  cfg.dynamicSmemBytes = UpdLayout<S>::total;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_dec_update<S>, a);
+  k_dec_step<S><<<grid, kDecThreads, DecLayout<S>::total, st>>>(a);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -375,7 +417,7 @@ int decode_step_multi(int n, const moc_decode_module* mods, int64_t B, int64_t D
   a.Dz = Dz;
   a.z = static_cast<const bf16*>(z);
   const int S = mods[0].kernel_size;
-  a.blk_prefix[0] = 0;
+  a.part_prefix[0] = 0;
   for (int i = 0; i < n; ++i) {
     DecModule& m = a.m[i];
     m.w = static_cast<const bf16*>(mods[i].weight);
@@ -388,33 +430,39 @@ int decode_step_multi(int n, const moc_decode_module* mods, int64_t B, int64_t D
     m.K = mods[i].n_bases;
     m.act = mods[i].activation;
     m.ract = mods[i].router_act;
-    a.blk_prefix[i + 1] = a.blk_prefix[i] + static_cast<int>(ceil_div(m.D, kUpdCh));
+    a.part_prefix[i + 1] = a.part_prefix[i] + static_cast<int>(ceil_div(ceil_div(m.D, kDecCh), kDecCluster));
   }
+  a.n_parts = a.part_prefix[n];
   if (B == 0) return MOC_OK;
+  const int64_t ctas = ceil_div(B, kDecTok) * a.n_parts * kDecCluster;
+  if (ctas > INT_MAX) return MOC_ERR_UNSUPPORTED_SHAPE;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return note_cuda(e);
-  if (dev < 0 || dev >= 64 || !g_dec_sm_configured[dev]) {
-    e = cudaFuncSetAttribute(k_dec_router, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecRouterSmem);
-    if (e != cudaSuccess) return note_cuda(e);
-    if (dev >= 0 && dev < 64) g_dec_sm_configured[dev] = 1;
-  }
-  k_dec_router<<<dim3(static_cast<unsigned>(ceil_div(B, kDecTok) * kDecCluster), static_cast<unsigned>(n)), 256,
-                 kDecRouterSmem, st>>>(a);
-  note_launch();
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return note_cuda(e);
-  const dim3 grid(static_cast<unsigned>(a.blk_prefix[n]), static_cast<unsigned>(ceil_div(B, kUpdTok)));
+  const unsigned grid = static_cast<unsigned>(ctas);
   switch (S) {
-    case 1: e = launch_update<1>(grid, a, st, dev); break;
-    case 2: e = launch_update<2>(grid, a, st, dev); break;
-    case 3: e = launch_update<3>(grid, a, st, dev); break;
-    case 4: e = launch_update<4>(grid, a, st, dev); break;
+    case 1: e = launch_step<1>(grid, a, st, dev); break;
+    case 2: e = launch_step<2>(grid, a, st, dev); break;
+    case 3: e = launch_step<3>(grid, a, st, dev); break;
+    case 4: e = launch_step<4>(grid, a, st, dev); break;
     default: return MOC_ERR_UNSUPPORTED_SHAPE;
   }
   if (e != cudaSuccess) return note_cuda(e);
   note_launch();
-  return note_cuda(cudaGetLastError());
+  return MOC_OK;
+}
+
+int decode_status(int* out, bool clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_dec_status, sizeof(int));
+  if (e != cudaSuccess) return note_cuda(e);
+  if (clear && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_dec_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return note_cuda(e);
+  }
+  *out = v;
+  return MOC_OK;
 }
 
 }  // namespace moc

@@ -72,6 +72,7 @@ int comm_status(int* out, bool clear);
 // by moc_device_status(); and a probe kernel that exercises the timeout path.
 int router_status(int* out, bool clear);
 int conv_status(int* out, bool clear);
+int decode_status(int* out, bool clear);
 int wait_timeout_probe(uint32_t limit, cudaStream_t st);
 
 constexpr int kMaxBasesSimt = 128;

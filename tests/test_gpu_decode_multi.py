@@ -99,7 +99,19 @@ def test_unfusable_modules_take_the_per_module_path():
     _run([(64, 32, "softmax", None), (64, 16, "exp", None)], B=3, z_dim=64, ks=4, steps=2)
 
 
-def test_fused_path_is_two_launches():
+def test_wide_modules_span_several_clusters():
+    # more than 1024 channels: several clusters per 16-token group, each routing the tokens
+    # itself; the last cluster of the first module has CTAs without channels
+    _run([(2056, 16, "exp", "silu"), (1160, 12, "softmax", None)], B=18, z_dim=264, ks=4, steps=2)
+
+
+def test_config4_shapes():
+    # the decode benchmark's modules: q D=4096, k / v D=1024, z_dim 4096, batch 128
+    _run([(4096, 16, "exp", None), (1024, 16, "exp", None), (1024, 16, "softmax", None)], B=128, z_dim=4096,
+         ks=4, steps=1)
+
+
+def test_fused_path_is_one_launch():
     mods = _modules([(512, 16, "exp", None), (128, 16, "exp", None), (128, 16, "softmax", None)], 256, 4, 9)
     B = 8
     caches = [torch.zeros(B, m.dim, 4, dtype=torch.bfloat16, device="cuda") for m in mods]
@@ -108,4 +120,4 @@ def test_fused_path_is_two_launches():
     n0 = _lib.launch_count()
     decode_step(mods, xs, z, caches)
     torch.cuda.synchronize()
-    assert _lib.launch_count() - n0 == 2
+    assert _lib.launch_count() - n0 == 1
