@@ -105,6 +105,12 @@ int moc_device_status(int* status, int clear);
  * staging kernels.  Used by the tests of the bounded-wait path. */
 int moc_wait_timeout_probe(uint32_t poll_limit, void* stream);
 
+/* Diagnostic: launches a cluster of two CTAs in which CTA 0 waits, with `poll_limit`
+ * polls and the fused decode step's cross-CTA wait, for bytes that CTA 1 never sends; it
+ * records MOC_STATUS_WAIT_TIMEOUT through the decode step's path and both CTAs leave
+ * through the cluster's exit barrier.  Used by the tests of the bounded-wait path. */
+int moc_cluster_wait_timeout_probe(uint32_t poll_limit, void* stream);
+
 /* Kernel family selection for every later call in this process: MOC_PATH_AUTO (tensor
  * cores for the bf16 shapes they support, the default) or MOC_PATH_GENERIC (the fp32
  * CUDA-core kernels for every shape).  Both compute the complete result; the switch

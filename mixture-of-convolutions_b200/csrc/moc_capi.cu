@@ -141,6 +141,10 @@ int moc_wait_timeout_probe(uint32_t poll_limit, void* stream) {
   return wait_timeout_probe(poll_limit, static_cast<cudaStream_t>(stream));
 }
 
+int moc_cluster_wait_timeout_probe(uint32_t poll_limit, void* stream) {
+  return decode_wait_timeout_probe(poll_limit, static_cast<cudaStream_t>(stream));
+}
+
 // Selects the kernel family: 0 = automatic (tensor cores where supported),
 // 1 = generic CUDA-core kernels for every shape.  Both compute the full result.
 int moc_set_kernel_path(int path) {

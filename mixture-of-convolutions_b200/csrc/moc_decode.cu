@@ -114,8 +114,8 @@ __device__ __forceinline__ void st_async_b32(uint32_t remote_addr, uint32_t remo
 }
 // Polls this CTA's mbarrier phase `parity` at most kSpinLimit times, with acquire at cluster
 // scope (the bytes it counts were written by other CTAs); true once the phase completed.
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, uint32_t limit = kSpinLimit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
@@ -395,6 +395,26 @@ __global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(kDecThread
   cluster_wait();  // no CTA of the cluster still stores into this one
 }
 
+// The decode step's cross-CTA wait with nothing to wait for: CTA 1 of the pair sends no
+// bytes, so CTA 0's wait runs out of polls and records the timeout; both CTAs then leave
+// through the exit barrier, as k_dec_step does.
+__global__ void __cluster_dims__(2, 1, 1) k_dec_wait_probe(uint32_t limit) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = smem_addr(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    mbar_expect_tx(b, 4);
+    fence_mbar_init();
+  }
+  cluster_arrive_relaxed();
+  cluster_wait();
+  bool ok = true;
+  if (cluster_rank() == 0) ok = mbar_wait_cluster(b, 0, limit);
+  if (!ok && threadIdx.x == 0) atomicOr(&g_dec_status, kStatusWaitTimeout);
+  cluster_arrive_relaxed();
+  cluster_wait();
+}
+
 template <int S>
 cudaError_t launch_step(unsigned grid, const DecArgs& a, cudaStream_t st, int dev) {
   static bool configured[64] = {};
@@ -450,6 +470,12 @@ int decode_step_multi(int n, const moc_decode_module* mods, int64_t B, int64_t D
   if (e != cudaSuccess) return note_cuda(e);
   note_launch();
   return MOC_OK;
+}
+
+int decode_wait_timeout_probe(uint32_t limit, cudaStream_t st) {
+  k_dec_wait_probe<<<2, 32, 0, st>>>(limit);
+  note_launch();
+  return note_cuda(cudaGetLastError());
 }
 
 int decode_status(int* out, bool clear) {

@@ -73,6 +73,7 @@ int comm_status(int* out, bool clear);
 int router_status(int* out, bool clear);
 int conv_status(int* out, bool clear);
 int decode_status(int* out, bool clear);
+int decode_wait_timeout_probe(uint32_t limit, cudaStream_t st);
 int wait_timeout_probe(uint32_t limit, cudaStream_t st);
 
 constexpr int kMaxBasesSimt = 128;

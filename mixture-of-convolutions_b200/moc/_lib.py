@@ -120,6 +120,7 @@ SIGNATURES = {
     "moc_launch_count": (ctypes.c_uint64, []),
     "moc_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     "moc_wait_timeout_probe": (ctypes.c_int, [ctypes.c_uint32, _P]),
+    "moc_cluster_wait_timeout_probe": (ctypes.c_int, [ctypes.c_uint32, _P]),
     "moc_forward": (ctypes.c_int, [_PROB, _P, _P, _P, _P, _P]),
     "moc_backward_workspace_bytes": (_SZ, [_PROB]),
     "moc_backward": (ctypes.c_int, [_PROB, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),

@@ -38,6 +38,7 @@ def _modules(specs, z_dim, ks, seed):
 
 
 def _run(specs, B, z_dim, ks, steps=4, prompt=9, seed=3):
+    _lib.device_status(clear=True)
     mods = _modules(specs, z_dim, ks, seed)
     g = torch.Generator().manual_seed(seed + 2)
     zp = torch.randn(B, prompt, z_dim, generator=g).bfloat16().cuda()
@@ -64,6 +65,7 @@ def _run(specs, B, z_dim, ks, steps=4, prompt=9, seed=3):
                                 m.activation, bf16_products=True)
                 assert rel_err(y[:, 0], yo) <= TOL
                 assert torch.equal(caches[i].double().cpu(), so)
+    assert _lib.device_status() == 0, "a decode wait ran out of polls"
 
 
 def test_qkv_shaped_modules():

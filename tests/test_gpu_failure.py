@@ -1,6 +1,7 @@
 """Failure detection on the GPU without a fault: the bounded mbarrier wait used by the
-TMA-staged kernels gives up after its poll budget, records MOC_STATUS_WAIT_TIMEOUT in
-the device status word, and returns; the CUDA context stays usable."""
+TMA-staged kernels, and the decode step's wait for another CTA's bytes, give up after
+their poll budget, record MOC_STATUS_WAIT_TIMEOUT in the device status word, and return;
+the CUDA context stays usable."""
 from __future__ import annotations
 
 import pytest
@@ -16,6 +17,18 @@ def test_wait_timeout_is_reported_not_hung():
     _lib.device_status(clear=True)
     stream = torch.cuda.current_stream().cuda_stream
     _lib.check(lib.moc_wait_timeout_probe(2000, stream), "moc_wait_timeout_probe")
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) & 1
+    assert _lib.device_status() == 0
+    t = torch.arange(8, device="cuda", dtype=torch.float32)
+    assert t.sum().item() == 28.0  # context still healthy
+
+
+def test_cluster_wait_timeout_is_reported_not_hung():
+    lib = _lib.load()
+    _lib.device_status(clear=True)
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.moc_cluster_wait_timeout_probe(2000, stream), "moc_cluster_wait_timeout_probe")
     torch.cuda.synchronize()
     assert _lib.device_status(clear=True) & 1
     assert _lib.device_status() == 0
