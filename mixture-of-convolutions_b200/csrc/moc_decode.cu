@@ -5,15 +5,17 @@
 // per module.  k_dec_step runs as clusters of 8 CTAs; a cluster covers 16 tokens and up to
 // 8 x 128 channels of one module (a module wider than 1024 channels takes several
 // clusters, each of which routes the 16 tokens itself).  Each CTA:
-//   1. starts the 16-byte copies of its update tiles (the basis slice of its 128 channels,
-//      x and the cache rows of its 16 tokens), none of which depend on the router;
-//   2. computes its share of the 16 x K router logits: warp w of CTA r owns the 32-column
-//      groups r*8 + w, r*8 + w + 64, ... of z_dim and reads them straight from global memory
-//      into mma.sync fragments (bf16 -> fp32), with no shared-memory staging;
-//   3. adds its warps' tiles in shared memory and stores the sum into CTA 0's shared memory
-//      (distributed shared memory); CTA 0 adds the 8 tiles in rank order, applies softmax /
-//      exp per token over 16 lanes (moc/api.py:383-388), writes alpha and stores its bf16
-//      value into the alpha tile of every CTA of the cluster;
+//   1. issues the loads of its share of the router operands: warp w of CTA r owns the
+//      32-column groups r*8 + w, r*8 + w + 64, ... of z_dim and reads them straight from
+//      global memory into mma.sync fragments, with no shared-memory staging; then starts the
+//      16-byte copies of its update tiles (the basis slice of its 128 channels, x and the
+//      cache rows of its 16 tokens), which are not needed before the router has finished;
+//   2. computes its share of the 16 x K router logits (bf16 -> fp32);
+//   3. adds its warps' tiles in shared memory and sends the sum to CTA 0 with st.async,
+//      which completes on CTA 0's mbarrier; CTA 0 adds the 8 tiles in rank order, applies
+//      softmax / exp per token over 16 lanes (moc/api.py:383-388), sends the bf16 alpha tile
+//      to the other CTAs the same way (each waits on its own mbarrier) and writes alpha to
+//      global memory;
 //   4. per tap, one ldmatrix of the basis and two mma.sync per warp form W_s = alpha . basis_s
 //      for 16 tokens x 16 channels (bf16 products exact, fp32 sums: the rounding of the
 //      reference's bf16 forward, moc/kernels.py:125-130; its decode kernel rounds each
