@@ -279,7 +279,9 @@ def run_decode(args, rank: int, world: int, local_rank: int) -> None:
     device = torch.device("cuda", local_rank)
     if world > 1:  # timing only: barrier and max over ranks
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
-    c = DECODE
+    c = dict(DECODE)
+    if args.batch is not None:
+        c["B"] = args.batch
     torch.manual_seed(77)
     mods, caches = [], []
     g = torch.Generator().manual_seed(78 + rank)
@@ -371,7 +373,7 @@ def run_decode(args, rank: int, world: int, local_rank: int) -> None:
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": "config4: decode, q D=4096 / k D=1024 / v D=1024, z_dim=4096, K=16, S=4, "
-                                   "batch 128, caches prefilled from a 512-token prompt",
+                                   f"batch {c['B']}, caches prefilled from a {c['prompt']}-token prompt",
                        "parallelism": f"replicas{world}",
                        "timing": "CUDA graph of one fused decode step (all modules) replayed K times; CUDA events"},
             "roofline": {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
@@ -636,8 +638,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
-                    help="sequences per rank for train / large / proj (a smaller case for ncu captures; "
-                         "default: the config's)")
+                    help="sequences per rank for train / large / proj / decode (a smaller case for ncu "
+                         "captures, or a decode batch sweep; default: the config's)")
     ap.add_argument("--workload", choices=("train", "decode", "varlen", "large", "proj"), default="train",
                     help="train: config 2 (the headline); decode: config 4, three modules, batch 128; "
                          "varlen: config 3, packed sequences, exp router, SiLU; large: config 5, "
