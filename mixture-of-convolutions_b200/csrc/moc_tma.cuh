@@ -1,7 +1,7 @@
 // Tensor Memory Accelerator (TMA) staging for sm_100a: 2-D tiled bulk copies
 // global -> shared completed on an mbarrier, with bounded waits.
 //
-// Loads here never use .multicast::cluster: each CTA fetches its own tiles.  Every wait
+// Loads here are never multicast across a cluster: each CTA fetches its own tiles.  Every wait
 // on an mbarrier gives up after kSpinLimit polls; the kernel then records an error in its
 // translation unit's device status word (read by moc_device_status()), waits once more,
 // again bounded, for the copies it issued, and returns.

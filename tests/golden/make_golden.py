@@ -41,8 +41,11 @@ def _np(t: torch.Tensor) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("MOC_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("MOC_REFERENCE"),
+                    help="the reference checkout (default: $MOC_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set MOC_REFERENCE to the reference checkout")
     sys.path.insert(0, args.reference)
     import moc as ref  # noqa: E402  (the reference package)
     import moc.api as ref_api  # noqa: E402
