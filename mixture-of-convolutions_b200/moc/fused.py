@@ -4,9 +4,10 @@ input, and the projection that feeds a module with the convolution as its epilog
 In the reference's attention block (README.md:120-129) the q, k and v short convolutions
 are three MoC modules routed by the same ``x_norm``.  Decoding one token through them one
 by one costs, per module, a router GEMM, its softmax / exp and the update kernel
-(moc/api.py:383-388, moc/ops.py:341-362).  ``decode_step`` runs all of them in two
-launches of ``moc_decode_step_multi``: one computes every module's router from one pass
-over z, the other mixes, convolves and shifts every module's cache.
+(moc/api.py:383-388, moc/ops.py:341-362).  ``decode_step`` runs all of them in one
+launch of ``moc_decode_step_multi``: clusters of CTAs compute each module's router, pass
+the routing weights between their CTAs on chip, then mix, convolve and shift every
+module's cache.
 
 Results match calling ``module.step(x, z, cache)`` for each module; shapes the fused
 kernels do not cover (fp32 or fp16 modules, more than 16 bases, kernel sizes above 4,
