@@ -342,6 +342,14 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
         atomicOr(&g_router_status, kStatusWaitTimeout);
         mbar_wait(bar0 + 8 * cur, parity);
       }
+      // this CTA's dW partial is incomplete: it is written as NaN, so the reduction of the
+      // partials (which reads every group) cannot return a finite mix of this call's and
+      // an earlier call's values
+      if (want_dw) {
+        for (int kn = 0; kn < 2 * KT; ++kn)
+          for (int e = 0; e < 4; ++e) dwa[kn][e] = __int_as_float(0x7fc00000);
+        break;
+      }
       return;
     }
     // every thread is past tile it-1, so its stage can be refilled with tile it+1
