@@ -316,6 +316,8 @@ __global__ void __launch_bounds__(256) k_router_dw_partial(int64_t N, int64_t Dz
 
 // Single block: exclusive scan of per-sequence chunk counts, then each thread writes
 // the (seq_id, chunk) pairs of its sequence (moc/ops.py:82-97 computes the same table).
+// Rows past the last chunk (a table sized by an upper bound, so that the host never reads
+// the offsets) are written as (-1, -1), which every kernel reads as an empty item.
 __global__ void __launch_bounds__(1024) k_chunk_indices(const void* cu, int cu_i64, int64_t n_seqs, int chunk,
                                                         int32_t* out, int64_t n_chunks) {
   __shared__ int64_t warp_tot[32];
@@ -351,6 +353,10 @@ __global__ void __launch_bounds__(1024) k_chunk_indices(const void* cu, int cu_i
     __syncthreads();
     if (threadIdx.x == blockDim.x - 1) carry = excl + cnt;
     __syncthreads();
+  }
+  for (int64_t o = carry + threadIdx.x; o < n_chunks; o += blockDim.x) {
+    out[2 * o] = -1;
+    out[2 * o + 1] = -1;
   }
 }
 
@@ -544,7 +550,7 @@ int simt_router_backward(int64_t N, int64_t Dz, int K, int dtype, int act, const
 
 int build_chunk_indices(const void* cu, int cu_i64, int64_t n_seqs, int chunk, int32_t* out, int64_t n_chunks,
                         cudaStream_t st) {
-  if (n_seqs == 0 || n_chunks == 0) return MOC_OK;
+  if (n_chunks == 0) return MOC_OK;
   k_chunk_indices<<<1, 1024, 0, st>>>(cu, cu_i64, n_seqs, chunk, out, n_chunks);
   note_launch();
   return note_cuda(cudaGetLastError());

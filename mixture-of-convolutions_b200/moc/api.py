@@ -146,7 +146,12 @@ class _MoCFunction(torch.autograd.Function):
                 cu_seqlens_cpu = cu_seqlens_cpu.contiguous()
             check_packed_inputs(x, alpha, basis, cu_seqlens, max_seqlen)
             if chunk_indices is None:
-                chunk_indices = ops.prepare_chunk_indices(cu_seqlens, cu_seqlens_cpu=cu_seqlens_cpu)
+                if cu_seqlens_cpu is not None:
+                    chunk_indices = ops.prepare_chunk_indices(cu_seqlens, cu_seqlens_cpu=cu_seqlens_cpu)
+                else:
+                    # the reference reads cu_seqlens on the host here (a stream sync,
+                    # moc/ops.py:82-97); a table sized by an upper bound needs no sync
+                    chunk_indices = ops.chunk_indices_upper_bound(cu_seqlens, x.shape[0])
             else:
                 chunk_indices = chunk_indices.contiguous()
         else:

@@ -103,6 +103,45 @@ def prepare_chunk_indices(
     return table
 
 
+def chunk_indices_upper_bound(cu_seqlens: torch.Tensor, n_tokens: int, chunk_size: int = VARLEN_BLOCK_T) -> torch.Tensor:
+    """int32 [n_tokens // chunk_size + n_seqs, 2] chunk table built on the device without
+    reading cu_seqlens on the host: no stream synchronisation, so a varlen forward and
+    backward can be captured in a CUDA graph.
+
+    The sum of ceil(len_i / chunk_size) over the n_seqs sequences of n_tokens tokens is at
+    most n_tokens // chunk_size + n_seqs, so a table of that many rows holds every chunk of
+    the reference's table (moc/ops.py:82-97), in the same order; the rows after the last
+    chunk are (-1, -1), which the kernels skip.  Outside stream capture the table is kept
+    in the same 4-entry LRU as ``prepare_chunk_indices``; during capture it is always built
+    in the graph's own memory, so the graph never depends on a table the LRU may drop.
+    """
+    n_seqs = cu_seqlens.numel() - 1
+    rows = int(n_tokens) // chunk_size + n_seqs
+    capturing = torch.cuda.is_current_stream_capturing()
+    key = ("bound", int(n_tokens))
+    version = _tensor_version(cu_seqlens)
+    if not capturing:
+        for pos, (c_cu, c_ver, c_size, c_cpu, c_cpu_ver, c_table) in enumerate(_chunk_index_cache):
+            if (c_cu is cu_seqlens and c_ver == version and c_size == chunk_size and isinstance(c_cpu, tuple)
+                    and c_cpu == key):
+                if pos:
+                    _chunk_index_cache.insert(0, _chunk_index_cache.pop(pos))
+                return c_table
+    table = torch.empty((rows, 2), dtype=torch.int32, device=cu_seqlens.device)
+    if rows > 0:
+        cu = cu_seqlens.contiguous()
+        with torch.cuda.device(cu.device):
+            rc = _lib.load().moc_prepare_chunk_indices(
+                _lib.ptr(cu), _lib.index_code(cu), n_seqs, chunk_size, _lib.ptr(table), rows,
+                _lib.stream_of(cu.device),
+            )
+        _lib.check(rc, "moc_prepare_chunk_indices")
+    if not capturing:
+        _chunk_index_cache.insert(0, (cu_seqlens, version, chunk_size, key, None, table))
+        del _chunk_index_cache[_CHUNK_CACHE_SIZE:]
+    return table
+
+
 def _aligned(t: torch.Tensor) -> torch.Tensor:
     """Contiguous and 16-byte aligned (the vectorised kernels stage rows in 16 B chunks)."""
     t = t.contiguous()
@@ -144,7 +183,10 @@ def _problem(
     keep: tuple = ()
     if cu_seqlens is not None:
         if chunk_indices is None:
-            chunk_indices = prepare_chunk_indices(cu_seqlens, block_t, cu_seqlens_cpu)
+            if cu_seqlens_cpu is not None:
+                chunk_indices = prepare_chunk_indices(cu_seqlens, block_t, cu_seqlens_cpu)
+            else:  # no host copy of the offsets: a bound-sized table, no device sync
+                chunk_indices = chunk_indices_upper_bound(cu_seqlens, x.shape[0], block_t)
         _check_chunk_indices(chunk_indices, cu_seqlens)
         cu = cu_seqlens.contiguous()
         p.batch = 0
