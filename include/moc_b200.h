@@ -180,12 +180,17 @@ int moc_router_backward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_
  * GPU that loads the library holds until the process exits.  Problems whose partials do
  * not fit return MOC_ERR_SCRATCH_LIMIT; other shapes and dtypes return
  * MOC_ERR_UNSUPPORTED_SHAPE / MOC_ERR_UNSUPPORTED_DTYPE.  The first call on a device looks
- * up the array's device address (cudaGetSymbolAddress), so make that first call before
- * any stream capture on that device.  All calls share the one array: calls that can
- * overlap on the GPU (different streams, or different host threads) race on it and must
- * be serialised by the caller.  Nothing in it needs to start at zero; every call rewrites
- * the partials it reads.  No counterpart in the reference (its router backward is PyTorch
- * autograd, which allocates through the caching allocator). */
+ * up the array's device address (cudaGetSymbolAddress) and keeps it for the life of the
+ * process, so make that first call before any stream capture on that device; the kept
+ * address does not survive cudaDeviceReset (which also frees every other allocation of
+ * the process), so do not call this after a reset.  All calls share the one array: calls
+ * that can overlap on the GPU (different streams, or different host threads) race on it
+ * and must be serialised by the caller.  Nothing in it needs to start at zero: every CTA
+ * writes its partial before the reduction reads it, and a CTA whose staging wait runs out
+ * (MOC_STATUS_WAIT_TIMEOUT, see moc_device_status) writes its partial as NaN, so dweight
+ * then comes out NaN instead of mixing in an earlier call's values.  No counterpart in the
+ * reference (its router backward is PyTorch autograd, which allocates through the caching
+ * allocator). */
 #define MOC_NOALLOC_SCRATCH_BYTES (8u << 20)
 int moc_router_backward_noalloc(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t dtype,
                                 int32_t router_act, const void* z, const void* weight,
@@ -194,8 +199,11 @@ int moc_router_backward_noalloc(int64_t n_tokens, int64_t z_dim, int32_t n_bases
 
 /* Device-side chunk index builder for packed varlen (no host sync): fills
  * chunk_indices [n_chunks, 2] int32 with (seq_id, chunk_in_seq) for every
- * chunk_size-token chunk of every sequence, in order.  n_chunks must equal
- * sum(ceil(len_i / chunk_size)); the caller computes it (e.g. from cu_seqlens_cpu).
+ * chunk_size-token chunk of every sequence, in order.  The exact table has
+ * sum(ceil(len_i / chunk_size)) rows.  A caller that does not know the lengths on the
+ * host (so never waits for the device) may pass any larger n_chunks, e.g. the bound
+ * n_tokens / chunk_size + n_seqs: the rows after the last chunk are written as (-1, -1),
+ * and moc_forward / moc_backward skip such rows.  A smaller n_chunks truncates the table.
  * Replaces the tensor arithmetic of prepare_chunk_indices, moc/ops.py:82-97. */
 int moc_prepare_chunk_indices(const void* cu_seqlens, int32_t cu_seqlens_dtype, int64_t n_seqs,
                               int32_t chunk_size, int32_t* chunk_indices, int64_t n_chunks,
@@ -297,9 +305,12 @@ int moc_proj_forward_multi(int32_t n_modules, const moc_proj_module* modules, in
  * arrays (data[i], counts[i] elements of dtypes[i]: fp32, fp16 or bf16), accumulating in
  * fp32 in rank order so every rank gets bitwise the same result.  Every rank must make
  * the same calls in the same order.  The call is stream-ordered and can be captured in a
- * CUDA graph.  A rank that waits too long for its peers records MOC_STATUS_WAIT_TIMEOUT
- * (see moc_device_status) and leaves its data unchanged.  No counterpart in the
- * reference, which trains in one process. */
+ * CUDA graph.  A rank that waits too long for its peers (more than the poll limit) records
+ * MOC_STATUS_WAIT_TIMEOUT in the communicator's status word (moc_comm_status) and in the
+ * library's (moc_device_status), and leaves its data unchanged.  The ranks' call counters
+ * then no longer pair up: before the next call, with no call in flight on any rank, every
+ * rank calls moc_comm_reset and waits for it (and for the others, e.g. a host barrier).
+ * No counterpart in the reference, which trains in one process. */
 #define MOC_COMM_MAX_RANKS 8
 #define MOC_COMM_MAX_SEGMENTS 4
 #define MOC_IPC_HANDLE_BYTES 64
@@ -309,6 +320,19 @@ int moc_comm_connect(moc_comm* comm, const void* handles);
 int moc_comm_allreduce(moc_comm* comm, int32_t n_segments, void* const* data, const int64_t* counts,
                        const int32_t* dtypes, void* stream);
 int moc_comm_destroy(moc_comm* comm);
+/* Polls of a peer's flag before a call gives up (0 restores the default, 2^22). */
+int moc_comm_set_poll_limit(moc_comm* comm, uint32_t poll_limit);
+/* This communicator's status word: MOC_STATUS_* bits of its calls since the last clear
+ * (synchronous: reads device memory). */
+int moc_comm_status(moc_comm* comm, int* status, int clear);
+/* Zeroes this rank's flags, call counters and status word (stream-ordered): the recovery
+ * after a timeout, described above. */
+int moc_comm_reset(moc_comm* comm, void* stream);
+/* Diagnostic: runs the all-reduce kernel as rank 0 of a world of two whose rank 1 never
+ * calls (on a fixed array of the library), so every wait gives up after poll_limit polls
+ * and records MOC_STATUS_WAIT_TIMEOUT (moc_device_status).  Used by the tests of the
+ * bounded-wait path. */
+int moc_comm_wait_timeout_probe(uint32_t poll_limit, void* stream);
 
 #ifdef __cplusplus
 }

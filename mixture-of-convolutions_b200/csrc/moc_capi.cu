@@ -297,6 +297,26 @@ int moc_comm_allreduce(moc_comm* comm, int32_t n_segments, void* const* data, co
                         static_cast<cudaStream_t>(stream));
 }
 
+int moc_comm_set_poll_limit(moc_comm* comm, uint32_t poll_limit) {
+  if (!comm) return MOC_ERR_INVALID_ARGUMENT;
+  comm_set_poll_limit(reinterpret_cast<CommImpl*>(comm), poll_limit);
+  return MOC_OK;
+}
+
+int moc_comm_status(moc_comm* comm, int* status, int clear) {
+  if (!comm || !status) return MOC_ERR_INVALID_ARGUMENT;
+  return comm_own_status(reinterpret_cast<CommImpl*>(comm), status, clear != 0);
+}
+
+int moc_comm_reset(moc_comm* comm, void* stream) {
+  if (!comm) return MOC_ERR_INVALID_ARGUMENT;
+  return comm_reset(reinterpret_cast<CommImpl*>(comm), static_cast<cudaStream_t>(stream));
+}
+
+int moc_comm_wait_timeout_probe(uint32_t poll_limit, void* stream) {
+  return comm_wait_timeout_probe(poll_limit, static_cast<cudaStream_t>(stream));
+}
+
 int moc_comm_destroy(moc_comm* comm) {
   if (!comm) return MOC_ERR_INVALID_ARGUMENT;
   return comm_destroy(reinterpret_cast<CommImpl*>(comm));

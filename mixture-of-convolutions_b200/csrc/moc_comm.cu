@@ -16,7 +16,12 @@
 //      rank, so the replicas stay bitwise identical) and writes it back in the gradient dtype.
 // CTAs only wait for the same CTA index on other GPUs, the grid is one wave, and the call
 // counter lives in device memory (CTA c keeps its own), so the launch can be captured in a
-// CUDA graph and replayed.  A wait that runs out records MOC_STATUS_WAIT_TIMEOUT.
+// CUDA graph and replayed.  A wait that runs out (after the communicator's poll limit)
+// records MOC_STATUS_WAIT_TIMEOUT in the communicator's status word and the library's, and
+// the CTA leaves its gradients unchanged.  After a timeout the ranks' call counters no
+// longer pair up (the timed-out call advanced them on some ranks only); comm_reset zeroes
+// this rank's counters, flags and status, and once every rank has reset, with no call in
+// flight anywhere, the next call pairs again.
 #include <algorithm>
 #include <cstring>
 
@@ -44,6 +49,8 @@ struct CommArgs {
   float* bufs[MOC_COMM_MAX_RANKS];        // every rank's exchange buffer (two halves of `cap` floats)
   uint32_t* flags[MOC_COMM_MAX_RANKS];    // every rank's flag array [kCommCtas][world]
   uint32_t* counter;                      // this rank's per-CTA call counters [kCommCtas]
+  int* status;                            // this communicator's status word
+  uint32_t poll_limit;                    // polls of a peer's flag before giving up
   CommSeg seg[MOC_COMM_MAX_SEGMENTS];
   int n_seg;
   int64_t total, cap;
@@ -113,9 +120,10 @@ __global__ void __launch_bounds__(kCommThreads) k_allreduce(const __grid_constan
     const uint32_t* f = a.flags[a.rank] + c * a.world + threadIdx.x;
     uint32_t n = 0;
     while (static_cast<int32_t>(ld_acquire_sys(f) - step) < 0) {
-      if (++n >= kCommPollLimit) {
+      if (++n >= a.poll_limit) {
         ok = 0;
         atomicOr(&g_comm_status, kStatusWaitTimeout);
+        atomicOr(a.status, kStatusWaitTimeout);
         break;
       }
       __nanosleep(32);
@@ -154,15 +162,19 @@ __global__ void __launch_bounds__(kCommThreads) k_allreduce(const __grid_constan
 struct CommImpl {
   int rank = 0, world = 0, device = -1;
   int64_t cap = 0;          // floats per buffer half
-  char* local = nullptr;    // this rank's allocation: [2 * cap floats | flags | counters]
+  uint32_t poll_limit = kCommPollLimit;
+  char* local = nullptr;    // this rank's allocation: [2 * cap floats | flags | counters | status]
   size_t local_bytes = 0;
   char* peers[MOC_COMM_MAX_RANKS] = {};  // opened IPC mappings (peers[rank] = local)
 };
 
-static size_t comm_layout(int64_t cap, int world, size_t* flags_off, size_t* counter_off) {
+// Byte offsets inside a rank's allocation; flags, counters and the status word are one
+// contiguous tail [flags_off, total), which comm_reset clears.
+static size_t comm_layout(int64_t cap, int world, size_t* flags_off, size_t* counter_off, size_t* status_off) {
   *flags_off = align_up(static_cast<size_t>(2 * cap) * sizeof(float), 256);
   *counter_off = align_up(*flags_off + static_cast<size_t>(kCommCtas) * world * sizeof(uint32_t), 256);
-  return align_up(*counter_off + kCommCtas * sizeof(uint32_t), 256);
+  *status_off = align_up(*counter_off + kCommCtas * sizeof(uint32_t), 256);
+  return align_up(*status_off + sizeof(int), 256);
 }
 
 int comm_create(int rank, int world, int64_t capacity, CommImpl** out, void* handle_out) {
@@ -171,8 +183,8 @@ int comm_create(int rank, int world, int64_t capacity, CommImpl** out, void* han
   c->world = world;
   c->cap = capacity;
   cudaError_t e = cudaGetDevice(&c->device);
-  size_t foff, coff;
-  c->local_bytes = comm_layout(capacity, world, &foff, &coff);
+  size_t foff, coff, soff;
+  c->local_bytes = comm_layout(capacity, world, &foff, &coff, &soff);
   if (e == cudaSuccess) e = cudaMalloc(&c->local, c->local_bytes);
   if (e == cudaSuccess) e = cudaMemset(c->local, 0, c->local_bytes);
   cudaIpcMemHandle_t h{};
@@ -205,14 +217,16 @@ int comm_connect(CommImpl* c, const void* handles) {
 int comm_allreduce(CommImpl* c, int n_seg, void* const* data, const int64_t* n, const int32_t* dtype,
                    cudaStream_t st) {
   CommArgs a{};
-  size_t foff, coff;
-  comm_layout(c->cap, c->world, &foff, &coff);
+  size_t foff, coff, soff;
+  comm_layout(c->cap, c->world, &foff, &coff, &soff);
   for (int r = 0; r < c->world; ++r) {
     if (c->peers[r] == nullptr) return MOC_ERR_INVALID_ARGUMENT;  // not connected
     a.bufs[r] = reinterpret_cast<float*>(c->peers[r]);
     a.flags[r] = reinterpret_cast<uint32_t*>(c->peers[r] + foff);
   }
   a.counter = reinterpret_cast<uint32_t*>(c->local + coff);
+  a.status = reinterpret_cast<int*>(c->local + soff);
+  a.poll_limit = c->poll_limit;
   a.n_seg = n_seg;
   a.total = 0;
   for (int s = 0; s < n_seg; ++s) {
@@ -243,6 +257,58 @@ int comm_destroy(CommImpl* c) {
   }
   delete c;
   return note_cuda(first);
+}
+
+void comm_set_poll_limit(CommImpl* c, uint32_t limit) { c->poll_limit = limit > 0 ? limit : kCommPollLimit; }
+
+int comm_reset(CommImpl* c, cudaStream_t st) {
+  size_t foff, coff, soff;
+  const size_t total = comm_layout(c->cap, c->world, &foff, &coff, &soff);
+  return note_cuda(cudaMemsetAsync(c->local + foff, 0, total - foff, st));
+}
+
+int comm_own_status(CommImpl* c, int* out, bool clear) {
+  size_t foff, coff, soff;
+  comm_layout(c->cap, c->world, &foff, &coff, &soff);
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, c->local + soff, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && clear && v != 0) e = cudaMemset(c->local + soff, 0, sizeof(int));
+  if (e != cudaSuccess) return note_cuda(e);
+  *out = v;
+  return MOC_OK;
+}
+
+// Probe of the timeout path: the all-reduce kernel, as rank 0 of a world of two whose
+// rank 1 never calls.  Both ranks' buffers and flag arrays are one fixed local array, so
+// rank 1's flags stay zero; every CTA waits `limit` polls, records the timeout and leaves
+// the probe data unchanged.
+__device__ float g_probe_buf[3 * 128];
+__device__ uint32_t g_probe_flags[kCommCtas * 2 + kCommCtas];
+__device__ int g_probe_status;
+
+int comm_wait_timeout_probe(uint32_t limit, cudaStream_t st) {
+  void *buf = nullptr, *flags = nullptr, *status = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&buf, g_probe_buf);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress(&flags, g_probe_flags);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress(&status, g_probe_status);
+  if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, sizeof(g_probe_flags), st);
+  if (e != cudaSuccess) return note_cuda(e);
+  CommArgs a{};
+  float* data = static_cast<float*>(buf) + 256;  // the "gradient": 128 floats after the two exchange halves
+  a.bufs[0] = a.bufs[1] = static_cast<float*>(buf);
+  a.flags[0] = a.flags[1] = static_cast<uint32_t*>(flags);
+  a.counter = static_cast<uint32_t*>(flags) + kCommCtas * 2;
+  a.status = static_cast<int*>(status);
+  a.poll_limit = limit > 0 ? limit : 1;
+  a.n_seg = 1;
+  a.seg[0] = CommSeg{data, 128, MOC_DTYPE_F32};
+  a.total = 128;
+  a.cap = 128;  // the exchange halves are buf[0, 128) and buf[128, 256)
+  a.rank = 0;
+  a.world = 2;
+  k_allreduce<<<kCommCtas, kCommThreads, 0, st>>>(a);
+  note_launch();
+  return note_cuda(cudaGetLastError());
 }
 
 int comm_status(int* out, bool clear) {

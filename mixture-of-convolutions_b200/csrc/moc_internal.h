@@ -67,6 +67,10 @@ int comm_allreduce(CommImpl* c, int n_seg, void* const* data, const int64_t* n, 
                    cudaStream_t st);
 int comm_destroy(CommImpl* c);
 int comm_status(int* out, bool clear);
+void comm_set_poll_limit(CommImpl* c, uint32_t limit);
+int comm_reset(CommImpl* c, cudaStream_t st);
+int comm_own_status(CommImpl* c, int* out, bool clear);
+int comm_wait_timeout_probe(uint32_t limit, cudaStream_t st);
 
 // device status words of the TMA-staged kernels (bounded-wait timeouts), read/cleared
 // by moc_device_status(); and a probe kernel that exercises the timeout path.

@@ -147,6 +147,10 @@ SIGNATURES = {
     "moc_comm_connect": (ctypes.c_int, [_P, _P]),
     "moc_comm_allreduce": (ctypes.c_int, [_P, _I32, ctypes.POINTER(_P), ctypes.POINTER(_I64), ctypes.POINTER(_I32), _P]),
     "moc_comm_destroy": (ctypes.c_int, [_P]),
+    "moc_comm_set_poll_limit": (ctypes.c_int, [_P, ctypes.c_uint32]),
+    "moc_comm_status": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    "moc_comm_reset": (ctypes.c_int, [_P, _P]),
+    "moc_comm_wait_timeout_probe": (ctypes.c_int, [ctypes.c_uint32, _P]),
 }
 
 COMM_MAX_RANKS = 8

@@ -97,6 +97,22 @@ class GradAllReduce:
 
 
 
+class CommTimeout(RuntimeError):
+    """A rank's all-reduce gave up waiting for its peers: that step's gradients were not
+    summed.  Raised on every rank by ``NVLinkGradAllReduce.check``, after the communicator
+    has been reset on every rank, so the next call pairs up again."""
+
+
+def all_ranks_ok(ok: bool, group=None, device: torch.device | None = None) -> bool:
+    """True on every rank when `ok` holds on every rank of `group` (one MIN all-reduce;
+    every rank must call it)."""
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32)
+    if dist.get_backend(group) == "nccl":
+        flag = flag.to(device if device is not None else torch.device("cuda", torch.cuda.current_device()))
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    return int(flag.item()) == 1
+
+
 class NVLinkGradAllReduce:
     """The same sum as GradAllReduce, by this library's own NVLink kernel instead of NCCL
     (``moc_comm_*`` in include/moc_b200.h): every rank's exchange buffer is opened by the
@@ -119,6 +135,7 @@ class NVLinkGradAllReduce:
         if world > _lib.COMM_MAX_RANKS:
             raise ValueError(f"at most {_lib.COMM_MAX_RANKS} ranks")
         self.device = dev
+        self.group = group
         self._comm = None
         lib = _lib.load()
         # every step of the setup ends with an agreement over `group`, so a failure on one
@@ -157,11 +174,7 @@ class NVLinkGradAllReduce:
         self._agree(ok, "the NVLink all-reduce self-check", _lib.MOC_OK, group)
 
     def _agree(self, ok: bool, what: str, rc: int, group) -> None:
-        flag = torch.tensor([1 if ok else 0], dtype=torch.int32)
-        if dist.get_backend(group) == "nccl":
-            flag = flag.to(self.device)
-        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
-        if int(flag.item()) == 1:
+        if all_ranks_ok(ok, group, self.device):
             return
         self.close(sync=False)
         if not ok:
@@ -185,6 +198,43 @@ class NVLinkGradAllReduce:
             _lib.check(_lib.load().moc_comm_allreduce(self._comm, n, ptrs, counts, dtypes,
                                                       _lib.stream_of(self.device)), "moc_comm_allreduce")
         return grads
+
+    def set_poll_limit(self, polls: int) -> None:
+        """Polls of a peer's flag before a call gives up (0: the default, 2^22)."""
+        _lib.check(_lib.load().moc_comm_set_poll_limit(self._comm, int(polls)), "moc_comm_set_poll_limit")
+
+    def status(self, clear: bool = False) -> int:
+        """MOC_STATUS_* bits this communicator's calls recorded (synchronous read)."""
+        v = ctypes.c_int(0)
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.load().moc_comm_status(self._comm, ctypes.byref(v), int(clear)), "moc_comm_status")
+        return v.value
+
+    def _sync(self) -> None:
+        torch.cuda.synchronize(self.device)
+
+    def reset(self) -> None:
+        """Zeroes this rank's flags, call counters and status (after a timeout, on every rank,
+        with no call in flight anywhere)."""
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.load().moc_comm_reset(self._comm, _lib.stream_of(self.device)), "moc_comm_reset")
+        torch.cuda.synchronize(self.device)
+
+    def check(self) -> None:
+        """Step-boundary check, made by every rank: raises CommTimeout on every rank if any
+        rank's call since the last check gave up waiting (its gradients were left unsummed).
+        Before raising, every rank resets its communicator and the ranks meet at a barrier,
+        so the next call pairs up again.  Synchronises this rank's device."""
+        self._sync()
+        bits = self.status(clear=True)
+        if all_ranks_ok(bits == 0, self.group, self.device):
+            return
+        self.reset()
+        dist.barrier(group=self.group)
+        raise CommTimeout(
+            "NVLink gradient all-reduce: a rank gave up waiting for its peers "
+            f"(this rank's status {bits:#x}); the gradients of the calls since the last check are not summed"
+        )
 
     def close(self, sync: bool = True) -> None:
         """Frees the exchange buffer (after every rank's last call has finished)."""

@@ -112,3 +112,58 @@ def test_two_gloo_ranks_reproduce_the_whole_batch_gradients(varlen):
     for r in range(world):
         _, _, rows, dx = res[r]
         torch.testing.assert_close(dx, dx_full[rows], rtol=1e-10, atol=1e-12)
+
+
+class _FakeComm(dp.NVLinkGradAllReduce):
+    """The step-boundary check of NVLinkGradAllReduce with the device calls replaced: each
+    rank reports the status bits `fail` says, and counts its resets."""
+
+    def __init__(self, bits: int):
+        self.group, self.device, self._comm = None, torch.device("cpu"), None
+        self.bits, self.resets = bits, 0
+
+    def _sync(self):
+        pass
+
+    def status(self, clear=False):
+        bits = self.bits
+        if clear:
+            self.bits = 0
+        return bits
+
+    def reset(self):
+        self.resets += 1
+        self.bits = 0
+
+
+def _check_main(rank: int, world: int, port: int, failing: int, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        comm = _FakeComm(1 if rank == failing else 0)
+        first = "ok"
+        try:
+            comm.check()
+        except dp.CommTimeout:
+            first = "raised"
+        second = "ok"
+        try:
+            comm.check()  # after the reset every rank is consistent again
+        except dp.CommTimeout:
+            second = "raised"
+        out[rank] = (first, second, comm.resets)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("failing", [-1, 0, 1], ids=["none", "rank0", "rank1"])
+def test_allreduce_timeout_raises_on_every_rank_and_resets_all(failing):
+    """A timeout seen by one rank makes every rank raise CommTimeout and reset (so the
+    ranks' call counters pair up again); with no timeout nobody raises or resets."""
+    world = 2
+    with mp.Manager() as mgr:
+        out = mgr.dict()
+        mp.spawn(_check_main, args=(world, _free_port(), failing, out), nprocs=world, join=True)
+        res = dict(out)
+    want = ("ok", "ok", 0) if failing < 0 else ("raised", "ok", 1)
+    assert all(res[r] == want for r in range(world)), res

@@ -125,3 +125,58 @@ def test_two_ranks_sum_and_agree():
         res = dict(out)
     for r in range(world):
         assert res[r] == (True, True, True, 0), res
+
+
+def _skip_rank_main(rank: int, world: int, port: int, out):
+    """Rank 1 skips one call of the all-reduce (between steps: none of its kernels is in
+    flight).  Rank 0's call gives up after a short poll limit; the step-boundary check
+    raises CommTimeout on both ranks and resets both communicators; the next call sums."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from moc import dp
+
+        ts = _tensors(rank, dev)
+        expect = []
+        for t in ts:
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t)
+            total = torch.zeros_like(t, dtype=torch.float32)
+            for p in parts:
+                total += p.float()
+            expect.append(total.to(t.dtype))
+        red = dp.NVLinkGradAllReduce(ts)
+        red.set_poll_limit(1 << 14)
+        skipped = [t.clone() for t in ts]
+        if rank == 0:
+            red(skipped)  # rank 1 makes no matching call
+        raised = False
+        try:
+            red.check()
+        except dp.CommTimeout:
+            raised = True
+        unchanged = all(torch.equal(s, t) for s, t in zip(skipped, ts))
+        red.set_poll_limit(0)
+        again = [t.clone() for t in ts]
+        red(again)
+        red.check()
+        summed = all(torch.equal(a, e) for a, e in zip(again, expect))
+        dist.barrier()
+        red.close()
+        out[rank] = (raised, unchanged, summed)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_skipped_call_times_out_raises_on_every_rank_and_recovers():
+    world = 2
+    with mp.Manager() as mgr:
+        out = mgr.dict()
+        mp.spawn(_skip_rank_main, args=(world, _free_port(), out), nprocs=world, join=True)
+        res = dict(out)
+    for r in range(world):
+        assert res[r] == (True, True, True), res

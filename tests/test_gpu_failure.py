@@ -47,3 +47,17 @@ def test_normal_kernels_record_no_timeouts():
     y.float().sum().backward()
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
+
+
+def test_allreduce_wait_timeout_is_reported_not_hung():
+    """The NVLink all-reduce kernel as rank 0 of two ranks whose rank 1 never calls: every
+    wait for rank 1's flag gives up after the given poll limit and records the timeout."""
+    lib = _lib.load()
+    _lib.device_status(clear=True)
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.moc_comm_wait_timeout_probe(4000, stream), "moc_comm_wait_timeout_probe")
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) & 1
+    assert _lib.device_status() == 0
+    t = torch.arange(8, device="cuda", dtype=torch.float32)
+    assert t.sum().item() == 28.0  # context still healthy
