@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """MoC forward+backward throughput on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ...]
 
 One step = the MoC module's training step on one batch of synthetic input: router
 (z @ router^T, softmax) -> convolution -> backward of both (dx, dz, dconv_bases,
@@ -12,15 +12,21 @@ init_std 0.002, router weight N(0, 0.02); x, z, dy ~ N(0, 1) from a seeded gener
                  and replayed K times with inputs resident in HBM (192 MiB of x, z, dy
                  per rank, larger than the 126 MB L2), timed with CUDA events.
 * ``e2e``        the same metric through the public API (``MoC`` forward + backward,
-                 eager), with x, z, dy copied from pinned host memory every step and
-                 y, dx, dz, dconv_bases, drouter copied back inside the timed region.
+                 eager), with x, z, dy copied from pinned host memory every step and the
+                 step's result, the parameter gradients dconv_bases and drouter, copied
+                 back, both inside the timed region (``h2d_bytes_per_step`` /
+                 ``d2h_bytes_per_step`` count exactly those copies).
 * ``roofline``   the dominant kernel timed alone (CUDA events on its stream):
                  algorithmic bytes per launch / average launch time vs measured HBM peak.
-* ``cpu_baseline`` the CPU oracle (a port of the reference's PyTorch path) on a bounded
-                 sample, rank 0 at N=1 only.
+* ``cpu_baseline`` the CPU oracle (a port of the reference's PyTorch path) on the full
+                 config-2 batch, rank 0 at N=1 only.
+* ``workloads``  (default workload, N=1) short runs of the other BASELINE workloads on
+                 the same GPU: config 3 (varlen), config 4 (decode) and config 5 (large,
+                 one GPU's share), each with its own value and roofline.
 
 With N > 1 (torchrun, one rank per GPU) every rank runs its own config-2 batch
-(weak scaling) and the step adds one NCCL all-reduce of [dconv_bases | drouter].
+(weak scaling) and the step adds one all-reduce of [dconv_bases | drouter]; after the
+timed region every rank checks that no all-reduce gave up waiting for a peer.
 ``--impl reference`` times the reference's CPU path (the oracle port) instead.
 """
 from __future__ import annotations
@@ -229,29 +235,38 @@ def barrier(world: int) -> None:
 
 # ----------------------------------------------------------------------------- CPU baseline
 
-def cpu_baseline(cfg: dict, iters: int = 2, seq_tokens: int = 2048) -> dict:
-    """The CPU oracle (a port of the reference's moc/reference.py + router, fp32) on one
-    sequence of `seq_tokens` tokens of the config, all host threads."""
+def cpu_baseline(cfg: dict, iters: int = 3, warmup: int = 1) -> dict:
+    """The CPU oracle (a port of the reference's moc/reference.py + router, fp32) on the
+    host's cores, all threads: config 2 on its full batch (B=4 x T=4096 tokens per step);
+    config 5 on one of its 4 sequences per GPU (8192 tokens), tokens/s scaled from that
+    sample.  Returns the mean over `iters` timed steps after `warmup` untimed ones."""
     from oracle import moc_oracle as O
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
+    large = cfg["D"] == CONFIG_LARGE["D"]
+    B = 1 if large else cfg["B"]
     g = torch.Generator().manual_seed(7)
-    x = torch.randn(1, seq_tokens, cfg["D"], generator=g)
-    z = torch.randn(1, seq_tokens, cfg["Dz"], generator=g)
-    dy = torch.randn(1, seq_tokens, cfg["D"], generator=g)
+    x = torch.randn(B, cfg["T"], cfg["D"], generator=g)
+    z = torch.randn(B, cfg["T"], cfg["Dz"], generator=g)
+    dy = torch.randn(B, cfg["T"], cfg["D"], generator=g)
     w = torch.randn(cfg["K"], cfg["Dz"], generator=g) * cfg["router_std"]
     b = (torch.rand(cfg["K"], cfg["S"], cfg["D"], generator=g) * 2 - 1) * cfg["init_std"] * 3 ** 0.5
-    O.module_grads(x, z, w, b, dy, cfg["router"], cfg["activation"], dtype=torch.float32)  # warm-up
-    times = []
-    for _ in range(iters):
-        t0 = time.perf_counter()
+    for _ in range(warmup):
         O.module_grads(x, z, w, b, dy, cfg["router"], cfg["activation"], dtype=torch.float32)
-        times.append(time.perf_counter() - t0)
-    t = statistics.median(times)
-    return {"value": seq_tokens / t, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"1 x {seq_tokens} tokens of the config, fp32 fwd+bwd, median of {iters} after 1 warm-up",
-            "sec_per_iter": t}
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        O.module_grads(x, z, w, b, dy, cfg["router"], cfg["activation"], dtype=torch.float32)
+    t = (time.perf_counter() - t0) / iters
+    tokens = B * cfg["T"]
+    if large:
+        sample = (f"1 of the config's {cfg['B']} sequences per GPU ({tokens} tokens), fp32 fwd+bwd, mean of {iters} "
+                  f"steps after {warmup} warm-up; tokens/s extrapolated from that sequence")
+    else:
+        sample = (f"the full config-2 batch ({B} x {cfg['T']} = {tokens} tokens per step), fp32 fwd+bwd, "
+                  f"mean of {iters} steps after {warmup} warm-up")
+    return {"value": tokens / t, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": sample, "sec_per_iter": t}
 
 
 DECODE = {"B": 128, "Dz": 4096, "K": 16, "S": 4, "prompt": 512,
@@ -268,7 +283,7 @@ def decode_bytes_per_step(c: dict) -> int:
     return total
 
 
-def run_decode(args, rank: int, world: int, local_rank: int) -> None:
+def run_decode(args, rank: int, world: int, local_rank: int) -> dict | None:
     """Config 4: q / k / v MoC modules sharing z, caches prefilled from a 512-token prompt,
     then one token per step for every sequence (replicas only for N > 1: each rank decodes
     its own batch, no collective)."""
@@ -365,9 +380,10 @@ def run_decode(args, rank: int, world: int, local_rank: int) -> None:
         del e2e_graph
     nbytes = decode_bytes_per_step(c)
     peaks = measured_peaks()
+    line = None
     if rank == 0:
         us = ms * 1e3
-        print(json.dumps({
+        line = {
             "metric": "MoC decode step latency (q, k, v modules)", "value": us, "unit": "us/step",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -388,12 +404,13 @@ def run_decode(args, rank: int, world: int, local_rank: int) -> None:
             "gpu_launches": launches_per_step * args.steps,
             "per_module_path_us": ms_per_module * 1e3,
             "clocks": clocks,
-        }), flush=True)
+        }
     sampler.stop()
     del graph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return line
 
 
 def varlen_lengths(total: int, seed: int) -> list[int]:
@@ -409,7 +426,7 @@ def varlen_lengths(total: int, seed: int) -> list[int]:
     return lens
 
 
-def run_varlen(args, rank: int, world: int, local_rank: int) -> None:
+def run_varlen(args, rank: int, world: int, local_rank: int) -> dict | None:
     """Config 3: 16384 packed tokens of sequences with lengths uniform in [64, 4096], D=Dz=2048,
     K=16, S=4, exp router, fused SiLU; one MoC fwd+bwd per step, captured in a CUDA graph.
     Each rank runs its own packed batch (weak scaling, no collective: replicas)."""
@@ -463,8 +480,9 @@ def run_varlen(args, rank: int, world: int, local_rank: int) -> None:
     clocks = sampler.summary(t0, t1)
     nbytes = step_bytes_per_token(D, D, K) * total
     peaks = measured_peaks()
+    line = None
     if rank == 0:
-        print(json.dumps({
+        line = {
             "metric": "MoC varlen fwd+bwd tokens/s", "value": total * world / (ms * 1e-3), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -478,19 +496,20 @@ def run_varlen(args, rank: int, world: int, local_rank: int) -> None:
                          "algorithmic_bytes_per_step": nbytes},
             "gpu_launches": launches * args.steps,
             "clocks": clocks,
-        }), flush=True)
+        }
     sampler.stop()
     del graph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return line
 
 
 PROJ = {"B": 4, "T": 4096, "d_model": 4096, "K": 16, "S": 4,
         "modules": (("q", 4096, "exp"), ("k", 1024, "exp"), ("v", 1024, "softmax"))}
 
 
-def run_proj(args, rank: int, world: int, local_rank: int) -> None:
+def run_proj(args, rank: int, world: int, local_rank: int) -> dict | None:
     """The fused projection + convolution forward: the q / k / v MoC modules of an attention
     block (README.md:115-129) at config 4's widths, prefill of B=4 x T=4096 tokens.  One step
     is the three routers and one moc_proj_forward_multi over qkv_proj.weight (h read once),
@@ -563,8 +582,9 @@ def run_proj(args, rank: int, world: int, local_rank: int) -> None:
     peaks = measured_peaks()
     peak_tf = peaks.get("bf16_tflops", FALLBACK_BF16_TFLOPS)
     tokens = B * T
+    line = None
     if rank == 0:
-        print(json.dumps({
+        line = {
             "metric": "MoC q/k/v projection + convolution prefill tokens/s", "value": tokens * world / (ms * 1e-3),
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -583,12 +603,13 @@ def run_proj(args, rank: int, world: int, local_rank: int) -> None:
                                  "per-sequence tile padding are extra work not counted"},
             "gpu_launches": launches * args.steps,
             "clocks": clocks,
-        }), flush=True)
+        }
     sampler.stop()
     del graph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return line
 
 
 def bench_config(cfg: dict, world: int) -> dict:
@@ -610,11 +631,13 @@ def bench_config(cfg: dict, world: int) -> dict:
 
 
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference arm: the reference's CPU path of the step (the oracle port of
+    moc/reference.py + the router, fp32) on the host's cores, K timed steps after W warm-up
+    steps, each the whole config-2 batch (config 5: one of its sequences).  Rank 0 only."""
     if rank != 0:
         return
     cfg = dict(CONFIG_LARGE if args.workload == "large" else CONFIG)
-    seq = 1024 if args.workload == "large" else 2048
-    base = cpu_baseline(cfg, iters=max(1, min(args.steps, 3)), seq_tokens=seq)
+    base = cpu_baseline(cfg, iters=args.steps, warmup=args.warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["sec_per_iter"] * 1e3,
@@ -623,7 +646,7 @@ def run_reference(args, rank: int, world: int) -> None:
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference CPU path: oracle port of moc/reference.py + router (the reference is Python; "
-                "its GPU path is Triton, not timed here)",
+                "its GPU path is Triton, timed separately in profiles/)",
     }
     print(json.dumps(line), flush=True)
 
@@ -637,6 +660,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra-workloads", action="store_true",
+                    help="with the default workload on one GPU, skip the short varlen / decode / large runs "
+                         "reported under the line's 'workloads' key")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per rank for train / large / proj / decode (a smaller case for ncu "
                          "captures, or a decode batch sweep; default: the config's)")
@@ -655,16 +681,33 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
-    if args.workload == "decode":
-        run_decode(args, rank, world, local_rank)
-        return
-    if args.workload == "varlen":
-        run_varlen(args, rank, world, local_rank)
-        return
-    if args.workload == "proj":
-        run_proj(args, rank, world, local_rank)
-        return
+    runners = {"train": run_train, "large": run_train, "decode": run_decode, "varlen": run_varlen, "proj": run_proj}
+    line = runners[args.workload](args, rank, world, local_rank)
+    if line is not None and args.workload == "train" and world == 1 and not args.no_extra_workloads:
+        # the other BASELINE workloads, short runs on the same GPU, reported in the same line
+        extra = {}
+        for name in ("varlen", "decode", "large"):
+            sub = argparse.Namespace(**vars(args))
+            sub.workload, sub.steps, sub.warmup, sub.batch = name, min(args.steps, 20), 3, None
+            sub.no_cpu_baseline = True
+            torch.cuda.empty_cache()
+            extra[name] = summarize(runners[name](sub, rank, world, local_rank))
+        line["workloads"] = extra
+    if line is not None:
+        print(json.dumps(line), flush=True)
 
+
+def summarize(line: dict) -> dict:
+    """The keys of a workload's line that the headline line carries for it."""
+    keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "higher_is_better", "config", "roofline",
+            "kernel_ms", "e2e", "per_module_path_us", "gpu_launches", "clocks", "step_hbm_frac")
+    return {k: line[k] for k in keep if k in line}
+
+
+def run_train(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """Config 2 (``--workload train``, the headline) or config 5 per GPU (``large``): the MoC
+    module's training step, one batch per rank (weak scaling); for N > 1 the step adds the one
+    all-reduce of [dconv_bases | drouter]."""
     from moc import _lib, dp
 
     torch.cuda.set_device(local_rank)
@@ -793,6 +836,8 @@ def main() -> None:
         gcopy = [g.clone() for g in g_grads[2:]]
         barrier(world)
         allreduce_ms = max_over_ranks(time_region(lambda: reducer(gcopy), 10, stream), world)
+    if hasattr(reducer, "check"):  # every rank: raises on all of them if any call gave up waiting
+        reducer.check()
     dominant = max(kernel_ms, key=kernel_ms.get)
     peaks = measured_peaks()
     kbytes = KERNEL_BYTES_PER_TOKEN[dominant](cfg) * N_rank
@@ -802,6 +847,7 @@ def main() -> None:
     step_bytes = step_bytes_per_token(cfg["D"], cfg["Dz"], cfg["K"]) * N_rank
     tokens_all = N_rank * world
 
+    line = None
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -835,9 +881,8 @@ def main() -> None:
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
-            base = cpu_baseline(cfg, seq_tokens=1024 if args.workload == "large" else 2048)
+            base = cpu_baseline(cfg)
             line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
-        print(json.dumps(line), flush=True)
 
     sampler.stop()
     del graph
@@ -847,6 +892,7 @@ def main() -> None:
             reducer.close()
         dist.barrier()
         dist.destroy_process_group()
+    return line
 
 
 def profiled_traffic(kernel: str):
