@@ -388,6 +388,15 @@ class MoC(nn.Module):
         cu_seqlens_cpu: Optional[torch.Tensor] = None,
         chunk_indices: Optional[torch.Tensor] = None,
     ) -> tuple[torch.Tensor, torch.Tensor | None]:
+        if (cache is not None and cu_seqlens is None and cu_seqlens_cpu is None and chunk_indices is None
+                and x.ndim == 3 and x.shape[1] == 1):
+            # a decode step: router and cache update in one launch where the fused kernel
+            # covers the shapes (bf16, k <= 16, kernel_size <= 4), else the path below
+            from .fused import step_one
+
+            y = step_one(self, x, z, cache)
+            if y is not None:
+                return y, (cache if output_final_state else None)
         alpha = _route(z, self.router, self.router_activation)
         return moc_triton(
             x,

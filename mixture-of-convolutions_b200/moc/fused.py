@@ -114,6 +114,29 @@ def decode_step(modules: Sequence[MoC], xs: Sequence[torch.Tensor], z: torch.Ten
     return [y.reshape(xo.shape) for y, xo in zip(ys, xs)]
 
 
+def step_one(module: MoC, x: torch.Tensor, z: torch.Tensor, cache: torch.Tensor) -> torch.Tensor | None:
+    """``module``'s decode step (x [B, 1, D], z [B, 1, z_dim], cache [B, D, S] updated in
+    place) as one launch of the fused kernel: the router and the update in the same CTAs,
+    where the per-module path launches the router, then the update.  Returns y [B, 1, D],
+    or None when the shapes are outside the fused kernel (the caller then takes the
+    per-module path).  Like the reference's step (moc/api.py:242-259), y carries no
+    gradient."""
+    if x.ndim != 3 or z.ndim != 3 or x.shape[1] != 1 or z.shape[1] != 1 or x.shape[0] != z.shape[0]:
+        return None
+    if x.shape[2] != module.dim or z.shape[2] != module.z_dim or cache.ndim != 3:
+        return None
+    if tuple(cache.shape) != (x.shape[0], module.dim, module.kernel_size):
+        return None
+    if not (x.is_cuda and z.is_cuda and cache.is_cuda and module.conv_bases.is_cuda):
+        return None
+    dev = x.device
+    if z.device != dev or cache.device != dev or module.conv_bases.device != dev or module.router.device != dev:
+        return None
+    if not _fusable([module], [x[:, 0]], z[:, 0], [cache]):
+        return None
+    return decode_step([module], [x], z, [cache])[0]
+
+
 def _proj_alpha(h: torch.Tensor, module: MoC, z: torch.Tensor | None, alpha: torch.Tensor | None) -> torch.Tensor:
     B, T = h.shape[:2]
     from . import ops

@@ -1,5 +1,7 @@
 """Fused multi-module decode (moc.fused.decode_step / moc_decode_step_multi) against the
-per-module path (MoC.step, i.e. router + moc_step) and the float64 oracle.
+unfused per-module path (router + moc_step, the reference's MoC.step lines) and the float64
+oracle.  MoC.step itself takes the fused kernel with one module where it covers the shapes;
+it is checked here against the same unfused path.
 
 Modules sharing z, with caches prefilled from a prompt, decode several tokens.  Per step:
 * the caches are bitwise equal to the per-module path's (they only move stored values);
@@ -14,8 +16,9 @@ from __future__ import annotations
 import pytest
 import torch
 
+import moc.ops as ops
 from conftest import rel_err
-from moc import MoC, _lib
+from moc import MoC, _lib, moc_triton
 from moc.fused import decode_step
 from oracle import moc_oracle as O
 
@@ -37,6 +40,13 @@ def _modules(specs, z_dim, ks, seed):
     return mods
 
 
+def _unfused_step(m, x, z, cache):
+    """The reference's step lines (moc/api.py:383-388, 242-259): the router launch, then
+    the cache update (moc_step), without the fused kernel."""
+    alpha = ops.launch_router_forward(z, m.router.detach(), m.router_activation)
+    return moc_triton(x, alpha, m.conv_bases.detach(), cache=cache, activation=m.activation)[0]
+
+
 def _run(specs, B, z_dim, ks, steps=4, prompt=9, seed=3):
     _lib.device_status(clear=True)
     mods = _modules(specs, z_dim, ks, seed)
@@ -53,7 +63,7 @@ def _run(specs, B, z_dim, ks, steps=4, prompt=9, seed=3):
             xs = [torch.randn(B, 1, m.dim, generator=g).bfloat16().cuda() for m in mods]
             before = [c.clone() for c in caches]
             ys = decode_step(mods, xs, z, caches)
-            refs = [m.step(x, z, c)[0] for m, x, c in zip(mods, xs, ref_caches)]
+            refs = [_unfused_step(m, x, z, c) for m, x, c in zip(mods, xs, ref_caches)]
             for i, (m, x, y, r) in enumerate(zip(mods, xs, ys, refs)):
                 assert y.shape == x.shape
                 assert torch.equal(caches[i], ref_caches[i]), f"module {i}: cache differs"
@@ -123,3 +133,31 @@ def test_fused_path_is_one_launch():
     decode_step(mods, xs, z, caches)
     torch.cuda.synchronize()
     assert _lib.launch_count() - n0 == 1
+
+
+@pytest.mark.parametrize("act,ract", [(None, "exp"), ("silu", "softmax")])
+def test_module_step_is_one_fused_launch(act, ract):
+    """MoC.step (the call unmodified reference code makes per module) runs the router and
+    the update as one launch, agrees with the unfused path within 2e-2 and moves the cache
+    bit for bit."""
+    m = _modules([(1024, 16, ract, act)], 512, 4, 21)[0]
+    B = 33
+    g = torch.Generator().manual_seed(22)
+    with torch.no_grad():
+        xp = torch.randn(B, 7, m.dim, generator=g).bfloat16().cuda()
+        zp = torch.randn(B, 7, 512, generator=g).bfloat16().cuda()
+        cache = m(xp, zp, output_final_state=True)[1].contiguous()
+        ref_cache = cache.clone()
+        for _ in range(3):
+            x = torch.randn(B, 1, m.dim, generator=g).bfloat16().cuda()
+            z = torch.randn(B, 1, 512, generator=g).bfloat16().cuda()
+            torch.cuda.synchronize()
+            n0 = _lib.launch_count()
+            y, out_cache = m.step(x, z, cache, output_final_state=True)
+            torch.cuda.synchronize()
+            assert _lib.launch_count() - n0 == 1
+            assert out_cache is cache and y.shape == x.shape
+            ref = _unfused_step(m, x, z, ref_cache)
+            assert torch.equal(cache, ref_cache)
+            assert rel_err(y, ref) <= TOL
+    assert _lib.device_status() == 0
