@@ -112,11 +112,14 @@ int moc_wait_timeout_probe(uint32_t poll_limit, void* stream);
 int moc_cluster_wait_timeout_probe(uint32_t poll_limit, void* stream);
 
 /* Kernel family selection for every later call in this process: MOC_PATH_AUTO (tensor
- * cores for the bf16 shapes they support, the default) or MOC_PATH_GENERIC (the fp32
- * CUDA-core kernels for every shape).  Both compute the complete result; the switch
- * exists so the two families can be cross-checked through this ABI. */
+ * cores for the bf16 shapes they support, the default; the convolution backward of 17..32
+ * bases with 5..8 taps takes its tcgen05 kernel), MOC_PATH_GENERIC (the fp32 CUDA-core
+ * kernels for every shape) or MOC_PATH_WARP_BACKWARD (as AUTO, but every tensor-core
+ * convolution backward takes the warp-level kernel).  All compute the complete result; the
+ * switch exists so the families can be cross-checked through this ABI. */
 #define MOC_PATH_AUTO 0
 #define MOC_PATH_GENERIC 1
+#define MOC_PATH_WARP_BACKWARD 2
 int moc_set_kernel_path(int path);
 
 /* Forward convolution: out = [silu](conv(x, alpha, basis)), out has x's dtype.

@@ -95,7 +95,7 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64
   return MOC_OK;
 }
 
-static bool use_tc(const moc_problem& p) { return g_kernel_path == 0 && tc_conv_supported(p); }
+static bool use_tc(const moc_problem& p) { return g_kernel_path != MOC_PATH_GENERIC && tc_conv_supported(p); }
 
 }  // namespace moc
 
@@ -129,6 +129,9 @@ int moc_device_status(int* status, int clear) {
   int r = 0, c = 0, m = 0, j = 0, d = 0;
   int rc = router_status(&r, clear != 0);
   if (rc == MOC_OK) rc = conv_status(&c, clear != 0);
+  int c5 = 0;
+  if (rc == MOC_OK) rc = bwd5_status(&c5, clear != 0);
+  c |= c5;
   if (rc == MOC_OK) rc = comm_status(&m, clear != 0);
   if (rc == MOC_OK) rc = proj_status(&j, clear != 0);
   if (rc == MOC_OK) rc = decode_status(&d, clear != 0);
@@ -145,11 +148,14 @@ int moc_cluster_wait_timeout_probe(uint32_t poll_limit, void* stream) {
   return decode_wait_timeout_probe(poll_limit, static_cast<cudaStream_t>(stream));
 }
 
-// Selects the kernel family: 0 = automatic (tensor cores where supported),
-// 1 = generic CUDA-core kernels for every shape.  Both compute the full result.
+// Selects the kernel family: automatic (tensor cores where supported), generic CUDA-core
+// kernels for every shape, or automatic with the warp-level conv backward for every shape.
+// All compute the full result.
 int moc_set_kernel_path(int path) {
-  if (path != 0 && path != 1) return MOC_ERR_INVALID_ARGUMENT;
+  if (path != MOC_PATH_AUTO && path != MOC_PATH_GENERIC && path != MOC_PATH_WARP_BACKWARD)
+    return MOC_ERR_INVALID_ARGUMENT;
   g_kernel_path = path;
+  tc_allow_bwd5(path == MOC_PATH_AUTO);
   return MOC_OK;
 }
 
@@ -331,14 +337,14 @@ int moc_router_forward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t
   if (n_tokens == 0) return MOC_OK;
   if (!z || !weight || !alpha) return MOC_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (g_kernel_path == 0 && tc_router_supported(n_tokens, z_dim, n_bases, dtype))
+  if (g_kernel_path != MOC_PATH_GENERIC && tc_router_supported(n_tokens, z_dim, n_bases, dtype))
     return tc_router_forward(n_tokens, z_dim, n_bases, router_act, z, weight, alpha, st);
   return simt_router_forward(n_tokens, z_dim, n_bases, dtype, router_act, z, weight, alpha, st);
 }
 
 size_t moc_router_backward_workspace_bytes(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t dtype) {
   if (n_tokens < 0 || z_dim <= 0 || n_bases <= 0) return 0;
-  if (g_kernel_path == 0 && tc_router_supported(n_tokens, z_dim, n_bases, dtype))
+  if (g_kernel_path != MOC_PATH_GENERIC && tc_router_supported(n_tokens, z_dim, n_bases, dtype))
     return tc_router_backward_ws(n_tokens, z_dim, n_bases);
   return simt_router_backward_ws(n_tokens, z_dim, n_bases);
 }
@@ -353,7 +359,7 @@ int moc_router_backward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_
   if (n_bases > kMaxBasesSimt) return MOC_ERR_UNSUPPORTED_SHAPE;
   if (n_tokens > 0 && (!z || !weight || !alpha || !dalpha)) return MOC_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (g_kernel_path == 0 && tc_router_supported(n_tokens, z_dim, n_bases, dtype)) {
+  if (g_kernel_path != MOC_PATH_GENERIC && tc_router_supported(n_tokens, z_dim, n_bases, dtype)) {
     if (workspace_bytes < tc_router_backward_ws(n_tokens, z_dim, n_bases)) return MOC_ERR_WORKSPACE_TOO_SMALL;
     return tc_router_backward(n_tokens, z_dim, n_bases, router_act, z, weight, alpha, dalpha, dalpha_dtype, dz,
                               dweight, workspace, workspace_bytes, st);

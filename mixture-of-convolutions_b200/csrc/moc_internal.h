@@ -37,6 +37,21 @@ size_t tc_backward_ws(const moc_problem& p);
 int tc_backward(const moc_problem& p, const void* x, const void* alpha, const void* basis, const void* dy,
                 void* dx, void* dalpha, void* dbasis, void* ws, size_t ws_bytes, cudaStream_t st);
 
+// fixed-order sum of the conv backward's per-CTA partials into dalpha / dbasis (moc_tc.cu)
+int tc_finalize(const float* da_part, int64_t n_slices, int64_t nk, void* dalpha, int adt, const float* db_part,
+                int64_t groups, int64_t ksd, void* dbasis, int bdt, cudaStream_t st);
+// lets tc_backward use the tcgen05 backward for the shapes it serves (default) or not
+void tc_allow_bwd5(bool allowed);
+
+// ---- conv backward with the dalpha / dbasis contractions on tcgen05 (moc_bwd5.cu), for the
+// bf16 shapes whose dbasis accumulators do not fit the warp-level kernel's registers
+// (17..32 bases, 5..8 taps)
+bool tc5_supported(const moc_problem& p);
+size_t tc5_backward_ws(const moc_problem& p);
+int tc5_backward(const moc_problem& p, const void* x, const void* alpha, const void* basis, const void* dy, void* dx,
+                 void* dalpha, void* dbasis, void* ws, size_t ws_bytes, cudaStream_t st);
+int bwd5_status(int* out, bool clear);
+
 // ---- tensor-core router for bf16 (moc_router_tc.cu)
 bool tc_router_supported(int64_t N, int64_t Dz, int K, int dtype);
 int tc_router_forward(int64_t N, int64_t Dz, int K, int act, const void* z, const void* w, void* alpha,

@@ -817,12 +817,8 @@ int bwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alph
   }
   note_launch();
   if (rc != MOC_OK) return rc;
-  const int64_t blocks = std::min<int64_t>(ceil_div(nk + ksd, 256), 8 * sm_count());
-  const cudaError_t e = launch_pdl(k_tc_finalize, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, args.da_part,
-                                   pl.slices, nk, dalpha, p.alpha_dtype, args.db_part, pl.groups, ksd, dbasis,
-                                   p.basis_dtype);
-  note_launch();
-  return note_cuda(e);
+  return tc_finalize(args.da_part, pl.slices, nk, dalpha, p.alpha_dtype, args.db_part, pl.groups, ksd, dbasis,
+                     p.basis_dtype, st);
 }
 
 template <template <int, int, bool> class F, typename... Args>
@@ -875,6 +871,21 @@ void ws_split(const moc_problem& p, int64_t& slices, int64_t& groups, size_t& da
 
 }  // namespace
 
+int tc_finalize(const float* da_part, int64_t n_slices, int64_t nk, void* dalpha, int adt, const float* db_part,
+                int64_t groups, int64_t ksd, void* dbasis, int bdt, cudaStream_t st) {
+  const int64_t blocks = std::min<int64_t>(ceil_div(nk + ksd, 256), 8 * sm_count());
+  const cudaError_t e = launch_pdl(k_tc_finalize, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, da_part,
+                                   n_slices, nk, dalpha, adt, db_part, groups, ksd, dbasis, bdt);
+  note_launch();
+  return note_cuda(e);
+}
+
+// Whether the shapes tc5_supported() covers take the tcgen05 backward (moc_bwd5.cu); off,
+// they take the two-pass warp-level backward below (moc_set_kernel_path(MOC_PATH_WARP_BACKWARD)).
+static bool g_bwd5_allowed = true;
+void tc_allow_bwd5(bool allowed) { g_bwd5_allowed = allowed; }
+static bool use_bwd5(const moc_problem& p) { return g_bwd5_allowed && tc5_supported(p); }
+
 bool tc_conv_supported(const moc_problem& p) {
   if (p.x_dtype != MOC_DTYPE_BF16 || p.alpha_dtype != MOC_DTYPE_BF16 || p.basis_dtype != MOC_DTYPE_BF16) return false;
   if (p.n_bases % 8 != 0 || p.n_bases > 32) return false;
@@ -900,6 +911,7 @@ int tc_forward(const moc_problem& p, const void* x, const void* alpha, const voi
 }
 
 size_t tc_backward_ws(const moc_problem& p) {
+  if (use_bwd5(p)) return tc5_backward_ws(p);
   int64_t slices, groups;
   size_t da, db;
   ws_split(p, slices, groups, da, db);
@@ -908,6 +920,7 @@ size_t tc_backward_ws(const moc_problem& p) {
 
 int tc_backward(const moc_problem& p, const void* x, const void* alpha, const void* basis, const void* dy, void* dx,
                 void* dalpha, void* dbasis, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (use_bwd5(p)) return tc5_backward(p, x, alpha, basis, dy, dx, dalpha, dbasis, ws, ws_bytes, st);
   if (!aligned16(x) || !aligned16(alpha) || !aligned16(basis) || !aligned16(dy) || (dx && !aligned16(dx)))
     return MOC_ERR_MISALIGNED;
   int64_t slices, groups;

@@ -232,5 +232,6 @@ def device_status(clear: bool = False) -> int:
 
 
 def set_kernel_path(path: int) -> None:
-    """0 = automatic (tensor-core kernels where supported), 1 = generic CUDA-core kernels."""
+    """0 = automatic (tensor-core kernels where supported), 1 = generic CUDA-core kernels,
+    2 = automatic with the warp-level convolution backward for every shape."""
     check(load().moc_set_kernel_path(path), "moc_set_kernel_path")

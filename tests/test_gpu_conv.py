@@ -56,7 +56,7 @@ def _assert_close(got, ref, xdt, label):
         assert err <= tol, f"{label} {name}: rel err {err:.3e} > {tol}"
 
 
-@pytest.fixture(params=[0, 1], ids=["auto", "generic"])
+@pytest.fixture(params=[0, 1, 2], ids=["auto", "generic", "warp_bwd"])
 def kernel_path(request):
     _lib.set_kernel_path(request.param)
     yield request.param
@@ -321,6 +321,42 @@ def test_many_bases_long_kernels_varlen(kernel_path):
     got, ref = _run(x[0], a[0], basis, dy[0], torch.bfloat16, torch.bfloat16, torch.bfloat16, None, cu=cu,
                     max_seqlen=max(lengths))
     _assert_close(got, ref, torch.bfloat16, "varlen K=32 S=8")
+
+
+@pytest.mark.parametrize("S", [5, 8])
+@pytest.mark.parametrize("act", [0, 1])
+@pytest.mark.parametrize("form", ["fixed", "varlen", "halo", "no_dx"])
+def test_tcgen05_and_warp_level_backward_agree(S, act, form):
+    """The two tensor-core backward kernels of 17..32 bases with 5..8 taps (the tcgen05 one,
+    MOC_PATH_AUTO, and the warp-level one, MOC_PATH_WARP_BACKWARD) on the same inputs: dx is
+    formed the same way in both (W_s on mma.sync, FFMA2 taps) and dalpha / dbasis differ only
+    in the order of their fp32 sums, so they agree to the rounding of the bf16 outputs."""
+    x, a, dy, basis = _inputs(2, 200, 384, 24, S, seed=31 + S)
+    kw, cu = {}, None
+    if form == "varlen":
+        cu = torch.tensor([0, 3, 70, 71, 199, 260, 400], dtype=torch.int32).cuda()
+        x, a, dy = x.reshape(1, 400, 384)[0], a.reshape(1, 400, 24)[0], dy.reshape(1, 400, 384)[0]
+        kw = {"cu_seqlens": cu}
+    if form == "halo":
+        kw = {"halo": torch.randn(2, 384, S).bfloat16().cuda()}
+    args = [t.bfloat16().cuda() for t in (x, a, basis)]
+    res = []
+    for path in (0, 2):
+        _lib.set_kernel_path(path)
+        try:
+            res.append(ops.launch_backward(*args, dy.bfloat16().cuda(), None, activation_flag=act,
+                                           need_x=form != "no_dx", **kw))
+        finally:
+            _lib.set_kernel_path(0)
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 0
+    (dx5, da5, db5), (dxw, daw, dbw) = res
+    if form == "no_dx":
+        assert dx5 is None and dxw is None
+    else:
+        assert rel_err(dx5, dxw) <= 1e-2
+    assert rel_err(da5, daw) <= 1e-2
+    assert rel_err(db5, dbw) <= 1e-2
 
 
 def test_generic_and_tensor_core_paths_agree():
