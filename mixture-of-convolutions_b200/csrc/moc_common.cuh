@@ -135,6 +135,24 @@ __device__ __forceinline__ float2 dsilu_bf2(float v0, float v1) {
   return __fmul2_rn(sig, __ffma2_rn(v, one_m, make_float2(1.f, 1.f)));
 }
 
+// ------------------------------------------------------------------ partial sums
+
+// Fixed-order sum of the `parts` partial rows (row p at base + p * stride) at element i, by the
+// four lanes sub = 0..3 of a lane quad (lanes 4m .. 4m + 3, all with the same i): lane sub adds
+// rows sub, sub + 4, ... in order, then the quad's four sums meet in a fixed shuffle tree, so
+// every call gives the same bits.  The shuffles name only the quad, so quads of one warp may
+// take different branches.  Four loads in flight per element where one lane would chain them.
+__device__ __forceinline__ float quad_part_sum(const float* __restrict__ base, int64_t parts, int64_t stride,
+                                               int64_t i, int sub) {
+  const unsigned quad = 0xfu << (threadIdx.x & 28);
+  float s = 0.f;
+#pragma unroll 4
+  for (int64_t p = sub; p < parts; p += 4) s += __ldg(base + p * stride + i);
+  s += __shfl_xor_sync(quad, s, 1);
+  s += __shfl_xor_sync(quad, s, 2);
+  return s;
+}
+
 // ------------------------------------------------------------------ row mapping
 
 // A work item is a run of consecutive token rows [r0, r1) inside one sequence whose

@@ -428,14 +428,14 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
   }
 }
 
+// out[i] = sum over the groups' dW partials (fixed order), four lanes per element
 __global__ void k_sum_groups(const float* __restrict__ part, int64_t groups, int64_t n, void* out, int dtype) {
   griddep_wait();  // the partials of the backward kernel
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float s = 0.f;
-#pragma unroll 8
-    for (int64_t g = 0; g < groups; ++g) s += __ldg(part + g * n + i);
-    st_any(out, dtype, i, s);
+  const int sub = threadIdx.x & 3;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x / 4;
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 4; i < n; i += step) {
+    const float s = quad_part_sum(part, groups, n, i, sub);
+    if (sub == 0) st_any(out, dtype, i, s);
   }
   griddep_launch_dependents();
 }
@@ -502,7 +502,7 @@ int bwd_kt(RouterBwdArgs& a, const void* z, int64_t slices, int64_t groups, void
   if (e != cudaSuccess) return note_cuda(e);
   if (dw != nullptr) {
     const int64_t n = static_cast<int64_t>(a.K) * a.Dz;
-    const int64_t blocks = std::min<int64_t>(ceil_div(n, 256), 4 * sm_count_r());
+    const int64_t blocks = std::min<int64_t>(ceil_div(4 * n, 256), 8 * sm_count_r());
     e = launch_pdl(k_sum_groups, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, a.dw_part, groups, n, dw,
                    static_cast<int>(MOC_DTYPE_BF16));
     note_launch();

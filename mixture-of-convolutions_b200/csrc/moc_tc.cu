@@ -341,8 +341,9 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
             mma_bf16(w[1], af[kt], bw[s][kt][2], bw[s][kt][3]);
           }
           uint32_t xr[4];
-          const int xrow = kHalo + 16 * b - j + lrow;
-          ldsm_x4(x_s + x_box + xrow * 128 + (((x_chunk ^ xrow) & 7) << 4), xr);
+          // row kHalo + 16 b - j + lrow: a 16-row step is 2048 bytes and leaves the swizzle term alone
+          const int xrow0 = kHalo - j + lrow;
+          ldsm_x4(x_s + x_box + xrow0 * 128 + (((x_chunk ^ xrow0) & 7) << 4) + b * 2048, xr);
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
             ffma2(acc[nt][0], acc[nt][1], w[nt][0], w[nt][1], bf_lo(xr[2 * nt]), bf_hi(xr[2 * nt]));
@@ -382,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
 template <int KT, int S, bool ACT, int PART>
 __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min_blocks))
     k_tc_bwd(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap dymap,
-             const __grid_constant__ CUtensorMap amap, TcArgs a) {
+             const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap dxmap, TcArgs a) {
   using L = Layout<KT, S, ACT, true, PART>;
   constexpr int KP = L::KP;
   constexpr bool BREG = L::BREG;
@@ -448,13 +449,16 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       if (threadIdx.x == 0) {
         atomicOr(&g_conv_status, kStatusWaitTimeout);
         mbar_wait(sm.bar + 8 * cur, parity);
+        bulk_wait<0>();
       }
       return;
     }
-    // every thread is past tile it-1, so its stage can be refilled with tile it+1
+    // every thread is past tile it-1, so its stage can be refilled with tile it+1 once the
+    // dx store of tile it-1 has read it
     if (threadIdx.x == 0 && it + 1 < i1) {
       int64_t ss, se, r0, r1;
       const uint32_t nbar = sm.bar + 8 * (cur ^ 1);
+      if constexpr (DXDA) bulk_wait_read<0>();
       if (a.rm.item(it + 1, ss, se, r0, r1))
         issue_tile<L, true>(&xmap, &dymap, &amap, sm.stages + (cur ^ 1) * L::stage_bytes, nbar, r0, ch_base);
       else
@@ -480,6 +484,10 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
     const uint32_t x_s = sm.stages + cur * L::stage_bytes;
     const uint32_t a_s = x_s + L::x_bytes + L::dy_bytes;
     const int rows = valid ? static_cast<int>(r1 - r0) : 0;
+    // dx of a whole tile leaves through the stage: block b's dx overwrites its dy rows (this
+    // warp's columns, which no later block reads), and one TMA store per box writes the tile.
+    // Shorter items store from registers.
+    const bool dx_tma = want_dx && rows == kTile;  // uniform across the CTA
     if (valid) {
       const int zx = static_cast<int>(std::min<int64_t>(std::max<int64_t>(ss - (r0 - kHalo), 0), L::XR));
       const int zdy = static_cast<int>(std::min<int64_t>(std::max<int64_t>(se - r0, 0), L::FR));
@@ -620,7 +628,11 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
           }
         }
       }
-      if (want_dx) {
+      if (dx_tma) {
+        __syncwarp();  // the warp's reads of these dy rows are done
+        stsm_x4(dy_addr(16 * b), pack_bf16(dxa[0][0], dxa[0][1]), pack_bf16(dxa[0][2], dxa[0][3]),
+                pack_bf16(dxa[1][0], dxa[1][1]), pack_bf16(dxa[1][2], dxa[1][3]));
+      } else if (want_dx) {
         bf16* dx_row = a.dx + (r0 + 16 * b + g) * a.D + ch_base + ch_w + 2 * q;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -644,18 +656,34 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
           *reinterpret_cast<float2*>(red + red_off<KP>(g + 8 * h, kn * 8 + 2 * q)) =
               make_float2(daa[kn][2 * h], daa[kn][2 * h + 1]);
       if (b % L::RB == L::RB - 1 || b == nb - 1) {
+        if (dx_tma && b == nb - 1) fence_proxy_async();  // this thread's dx rows, before the store
         __syncthreads();
+        if (dx_tma && b == nb - 1 && threadIdx.x == 0) {
+          tma_store_2d(&dxmap, static_cast<int>(ch_base), static_cast<int>(r0), x_s + L::x_bytes);
+          if (ch_base + 64 < a.D)
+            tma_store_2d(&dxmap, static_cast<int>(ch_base) + 64, static_cast<int>(r0), x_s + L::x_bytes + L::dybox);
+          bulk_commit();
+        }
+        // four consecutive bases of one token row per thread: 16-byte loads of the 8 warps'
+        // partials (red_off keeps aligned groups of four together), added in warp order
         const int b0 = b - b % L::RB;
         const int n_out = (b - b0 + 1) * 16 * KP;
-        for (int o = threadIdx.x; o < n_out; o += kThreads) {
+        for (int o = 4 * threadIdx.x; o < n_out; o += 4 * kThreads) {
           const int blk = o / (16 * KP), rem = o - blk * 16 * KP;
           const int row = rem / KP, k = rem - row * KP;
           const float* rb = red_s + blk * 8 * 16 * KP + red_off<KP>(row, k);
-          float sum = 0.f;
+          float4 sum = *reinterpret_cast<const float4*>(rb);
 #pragma unroll
-          for (int w = 0; w < 8; ++w) sum += rb[w * 16 * KP];
+          for (int w = 1; w < 8; ++w) {
+            const float4 v = *reinterpret_cast<const float4*>(rb + w * 16 * KP);
+            const float2 lo = __fadd2_rn(make_float2(sum.x, sum.y), make_float2(v.x, v.y));
+            const float2 hi = __fadd2_rn(make_float2(sum.z, sum.w), make_float2(v.z, v.w));
+            sum = make_float4(lo.x, lo.y, hi.x, hi.y);
+          }
           const int trow = 16 * (b0 + blk) + row;
-          if (k < a.K && trow < rows) a.da_part[(slice * a.n_tokens + r0 + trow) * a.K + k] = sum;
+          // K % 8 == 0 on this path: a group of four is all valid or all padding
+          if (k < a.K && trow < rows)
+            *reinterpret_cast<float4*>(a.da_part + (slice * a.n_tokens + r0 + trow) * a.K + k) = sum;
         }
         if (b < nb - 1) __syncthreads();  // red_s is rewritten by the next blocks of this tile
       }
@@ -663,6 +691,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
     // the next iteration's wait barrier orders these reads of red_s and the stage before reuse
   }
 
+  if (DXDA && threadIdx.x == 0) bulk_wait<0>();  // the last dx stores
   griddep_launch_dependents();  // only the dbasis partial store is left
   // dbasis partial of this CTA: db_part[group][k][s][ch]
   if constexpr (!DB) return;
@@ -744,14 +773,16 @@ int configure(const void* kern, bool (&configured)[64], int smem) {
 }
 
 struct Maps {
-  CUtensorMap x, dy, a;
+  CUtensorMap x, dy, a, dx;
 };
 
 template <class L, bool BWD>
-int make_maps(const moc_problem& p, const void* x, const void* dy, const void* alpha, Maps& m) {
+int make_maps(const moc_problem& p, const void* x, const void* dy, const void* alpha, const void* dx, Maps& m) {
   const uint64_t D = static_cast<uint64_t>(p.dim), N = static_cast<uint64_t>(p.n_tokens);
   int rc = make_tmap_bf16_2d(&m.x, x, D, N, D * 2, 64, L::XR, 128);
   if (rc == MOC_OK && BWD) rc = make_tmap_bf16_2d(&m.dy, dy, D, N, D * 2, 64, L::FR, 128);
+  // dx: stored from the dy area of the stage, 64 rows at a time (a map of dy when there is no dx)
+  if (rc == MOC_OK && BWD) rc = make_tmap_bf16_2d(&m.dx, dx != nullptr ? dx : dy, D, N, D * 2, 64, kTile, 128);
   if (rc == MOC_OK)  // alpha rows of KP bases (32 or 64 bytes), swizzled over their span
     rc = make_tmap_bf16_2d(&m.a, alpha, static_cast<uint64_t>(p.n_bases), N, static_cast<uint64_t>(p.n_bases) * 2,
                            L::KP, L::AR, L::ARB);
@@ -769,7 +800,7 @@ int fwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alph
   int rc = configure(reinterpret_cast<const void*>(k_tc_fwd<KT, S, ACT>), configured, L::total);
   if (rc != MOC_OK) return rc;
   Maps m;
-  rc = make_maps<L, false>(p, x, nullptr, alpha, m);
+  rc = make_maps<L, false>(p, x, nullptr, alpha, nullptr, m);
   if (rc != MOC_OK) return rc;
   const cudaError_t e = launch_pdl(k_tc_fwd<KT, S, ACT>, dim3(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups)),
                                    dim3(kThreads), L::total, st, m.x, m.a, args);
@@ -803,17 +834,17 @@ int bwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alph
   }
   if (rc != MOC_OK) return rc;
   Maps m;
-  rc = make_maps<L, true>(p, x, dy, alpha, m);
+  rc = make_maps<L, true>(p, x, dy, alpha, args.dx, m);
   if (rc != MOC_OK) return rc;
   const dim3 grid(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups));
   if constexpr (bwd_split(KT, S)) {
-    rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdDxDa>, grid, dim3(kThreads), L::total, st, m.x, m.dy, m.a, args));
+    rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdDxDa>, grid, dim3(kThreads), L::total, st, m.x, m.dy, m.a, m.dx, args));
     note_launch();
     if (rc != MOC_OK) return rc;
     rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdDb>, grid, dim3(kThreads), Layout<KT, S, ACT, true, kBwdDb>::total,
-                              st, m.x, m.dy, m.a, args));
+                              st, m.x, m.dy, m.a, m.dx, args));
   } else {
-    rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdAll>, grid, dim3(kThreads), L::total, st, m.x, m.dy, m.a, args));
+    rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdAll>, grid, dim3(kThreads), L::total, st, m.x, m.dy, m.a, m.dx, args));
   }
   note_launch();
   if (rc != MOC_OK) return rc;
