@@ -214,7 +214,8 @@ __device__ __forceinline__ void fill_halo(char* stage, const RowMap& rm, int64_t
 
 template <int KT, int S, bool ACT>
 __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_blocks))
-    k_tc_fwd(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap amap, TcArgs a) {
+    k_tc_fwd(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap amap,
+             const __grid_constant__ CUtensorMap ymap, TcArgs a) {
   using L = Layout<KT, S, ACT, false>;
   extern __shared__ __align__(1024) char smem_raw[];
   const Smem<L> sm(smem_raw);
@@ -281,13 +282,16 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
       if (threadIdx.x == 0) {
         atomicOr(&g_conv_status, kStatusWaitTimeout);
         mbar_wait(sm.bar + 8 * cur, parity);
+        bulk_wait<0>();
       }
       return;
     }
-    // every thread is past tile it-1, so its stage can be refilled with tile it+1
+    // every thread is past tile it-1, so its stage can be refilled with tile it+1 once the
+    // y store of tile it-1 has read it
     if (threadIdx.x == 0 && it + 1 < i1) {
       int64_t ss, se, r0, r1;
       const uint32_t nbar = sm.bar + 8 * (cur ^ 1);
+      bulk_wait_read<0>();
       if (a.rm.item(it + 1, ss, se, r0, r1))
         issue_tile<L, false>(&xmap, nullptr, &amap, sm.stages + (cur ^ 1) * L::stage_bytes, nbar, r0, ch_base);
       else
@@ -322,6 +326,11 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
       const uint32_t a_s = x_s + L::x_bytes;
       const int rows = static_cast<int>(r1 - r0);
       const int nb = (rows + 15) >> 4;
+      // y of a whole tile leaves through the stage: block b's outputs overwrite x rows 16 b ..
+      // 16 b + 15 of this warp's columns, which only blocks up to b read (block b + 1 starts
+      // at row 16 b + 17), and one TMA store per box writes the tile.  Shorter items store
+      // through the warp's staging rows.
+      const bool y_tma = rows == kTile;  // uniform across the CTA
       bf16* out_tile = a.out + r0 * a.D + ch_stage;
 #pragma unroll 1
       for (int b = 0; b < nb; ++b) {
@@ -364,7 +373,12 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
           }
           o[i] = pack_bf16(v0, v1);
         }
-        __syncwarp();  // the previous block's staging rows have been read
+        __syncwarp();  // the previous block's staging rows / this block's x rows have been read
+        if (y_tma) {
+          const int yr = 16 * b + lrow;
+          stsm_x4(x_s + x_box + yr * 128 + (((x_chunk ^ yr) & 7) << 4), o[0], o[1], o[2], o[3]);
+          continue;
+        }
         stsm_x4(ost_w + lrow * 32 + ((((lane >> 4) ^ (lrow >> 2)) & 1) << 4), o[0], o[1], o[2], o[3]);
         __syncwarp();
         {
@@ -374,8 +388,18 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, false>::min_bloc
             *reinterpret_cast<uint4*>(out_tile + (16 * b + row) * a.D + half * 8) = v;
         }
       }
+      if (y_tma) {
+        fence_proxy_async();  // this thread's y rows, before the store
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          tma_store_2d(&ymap, static_cast<int>(ch_base), static_cast<int>(r0), x_s);
+          if (ch_base + 64 < a.D) tma_store_2d(&ymap, static_cast<int>(ch_base) + 64, static_cast<int>(r0), x_s + L::xbox);
+          bulk_commit();
+        }
+      }
     }
   }
+  if (threadIdx.x == 0) bulk_wait<0>();  // the last y stores
 }
 
 // ------------------------------------------------------------------ backward
@@ -773,7 +797,7 @@ int configure(const void* kern, bool (&configured)[64], int smem) {
 }
 
 struct Maps {
-  CUtensorMap x, dy, a, dx;
+  CUtensorMap x, dy, a, out;  // out: the TMA-stored output, dx (backward) or y (forward)
 };
 
 template <class L, bool BWD>
@@ -782,7 +806,7 @@ int make_maps(const moc_problem& p, const void* x, const void* dy, const void* a
   int rc = make_tmap_bf16_2d(&m.x, x, D, N, D * 2, 64, L::XR, 128);
   if (rc == MOC_OK && BWD) rc = make_tmap_bf16_2d(&m.dy, dy, D, N, D * 2, 64, L::FR, 128);
   // dx: stored from the dy area of the stage, 64 rows at a time (a map of dy when there is no dx)
-  if (rc == MOC_OK && BWD) rc = make_tmap_bf16_2d(&m.dx, dx != nullptr ? dx : dy, D, N, D * 2, 64, kTile, 128);
+  if (rc == MOC_OK && BWD) rc = make_tmap_bf16_2d(&m.out, dx != nullptr ? dx : dy, D, N, D * 2, 64, kTile, 128);
   if (rc == MOC_OK)  // alpha rows of KP bases (32 or 64 bytes), swizzled over their span
     rc = make_tmap_bf16_2d(&m.a, alpha, static_cast<uint64_t>(p.n_bases), N, static_cast<uint64_t>(p.n_bases) * 2,
                            L::KP, L::AR, L::ARB);
@@ -801,9 +825,13 @@ int fwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alph
   if (rc != MOC_OK) return rc;
   Maps m;
   rc = make_maps<L, false>(p, x, nullptr, alpha, nullptr, m);
+  // y: stored from the x area of the stage, 64 rows at a time
+  if (rc == MOC_OK)
+    rc = make_tmap_bf16_2d(&m.out, args.out, static_cast<uint64_t>(p.dim), static_cast<uint64_t>(p.n_tokens),
+                           static_cast<uint64_t>(p.dim) * 2, 64, kTile, 128);
   if (rc != MOC_OK) return rc;
   const cudaError_t e = launch_pdl(k_tc_fwd<KT, S, ACT>, dim3(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups)),
-                                   dim3(kThreads), L::total, st, m.x, m.a, args);
+                                   dim3(kThreads), L::total, st, m.x, m.a, m.out, args);
   note_launch();
   return note_cuda(e);
 }
@@ -838,13 +866,13 @@ int bwd_inst(const moc_problem& p, TcArgs& args, const void* x, const void* alph
   if (rc != MOC_OK) return rc;
   const dim3 grid(static_cast<unsigned>(pl.slices), static_cast<unsigned>(pl.groups));
   if constexpr (bwd_split(KT, S)) {
-    rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdDxDa>, grid, dim3(kThreads), L::total, st, m.x, m.dy, m.a, m.dx, args));
+    rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdDxDa>, grid, dim3(kThreads), L::total, st, m.x, m.dy, m.a, m.out, args));
     note_launch();
     if (rc != MOC_OK) return rc;
     rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdDb>, grid, dim3(kThreads), Layout<KT, S, ACT, true, kBwdDb>::total,
-                              st, m.x, m.dy, m.a, m.dx, args));
+                              st, m.x, m.dy, m.a, m.out, args));
   } else {
-    rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdAll>, grid, dim3(kThreads), L::total, st, m.x, m.dy, m.a, m.dx, args));
+    rc = note_cuda(launch_pdl(k_tc_bwd<KT, S, ACT, kBwdAll>, grid, dim3(kThreads), L::total, st, m.x, m.dy, m.a, m.out, args));
   }
   note_launch();
   if (rc != MOC_OK) return rc;
