@@ -209,7 +209,8 @@ struct RouterBwdArgs {
 // 128B-swizzled boxes) on mbarriers; every thread computes dlogits for the next tile's
 // tokens meanwhile.
 template <int KT>
-__global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ CUtensorMap zmap, RouterBwdArgs a) {
+__global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ CUtensorMap zmap,
+                                                      const __grid_constant__ CUtensorMap dzmap, RouterBwdArgs a) {
   using L = BwdLayout<KT>;
   constexpr int KP = L::KP;
   extern __shared__ __align__(1024) char smem_raw[];
@@ -341,6 +342,7 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
       if (threadIdx.x == 0) {
         atomicOr(&g_router_status, kStatusWaitTimeout);
         mbar_wait(bar0 + 8 * cur, parity);
+        bulk_wait<0>();
       }
       // this CTA's dW partial is incomplete: it is written as NaN, so the reduction of the
       // partials (which reads every group) cannot return a finite mix of this call's and
@@ -352,16 +354,25 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
       }
       return;
     }
-    // every thread is past tile it-1, so its stage can be refilled with tile it+1
-    if (threadIdx.x == 0 && it + 1 < i1) issue(it + 1, cur ^ 1);
+    // every thread is past tile it-1, so its stage can be refilled with tile it+1 once the
+    // dz store of tile it-1 has read it
+    if (threadIdx.x == 0 && it + 1 < i1) {
+      bulk_wait_read<0>();
+      issue(it + 1, cur ^ 1);
+    }
     const uint32_t z_s = z_st + cur * L::z_bytes;
     const int64_t tok0 = it * kBwdTile;
+    // dz of a whole tile leaves through the stage: block b's dz overwrites its z rows (this
+    // warp's columns) once the block's dW products have read them, and one TMA store per box
+    // writes the tile.  A partial last tile stores through the warp's staging rows.
+    const bool dz_tma = want_dz && a.vec_dz && tok0 + kBwdTile <= a.N;  // uniform across the CTA
     for (int b = 0; b < kBwdTile / 16; ++b) {
       if (tok0 + 16 * b >= a.N) break;
       uint32_t af[KT][4];  // dl rows of this block (A operand of dz)
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt)
         ldsm_x4(smem_addr(dl_cur + (16 * b + lm_row(lane)) * L::DLB + (kt * 16 + lm_col(lane)) * 2), af[kt]);
+      uint32_t dzp[4];  // this block's dz (stmatrix order) when the tile leaves by TMA
       if (want_dz) {
         // dz[tok, col] = sum_k dl[tok, k] W[k, col]
         float acc[2][4];
@@ -372,7 +383,10 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
           mma_bf16(acc[0], af[kt], wb[kt][0], wb[kt][1]);
           mma_bf16(acc[1], af[kt], wb[kt][2], wb[kt][3]);
         }
-        if (a.vec_dz) {
+        if (dz_tma) {
+          dzp[0] = pack_bf16(acc[0][0], acc[0][1]), dzp[1] = pack_bf16(acc[0][2], acc[0][3]);
+          dzp[2] = pack_bf16(acc[1][0], acc[1][1]), dzp[3] = pack_bf16(acc[1][2], acc[1][3]);
+        } else if (a.vec_dz) {
           // the block's 16 x 16 dz go through the warp's staging rows (stmatrix) and leave
           // as one 16-byte store per lane (a full 32-byte row segment per lane pair)
           const int lr = lm_row(lane);
@@ -412,8 +426,24 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
           mma_bf16(dwa[2 * kt + 1], zt, db[2], db[3]);
         }
       }
+      if (dz_tma) {
+        __syncwarp();  // the warp's dW reads of these z rows are done
+        const int r = 16 * b + lm_row(lane);
+        stsm_x4(z_s + zt_box + r * 128 + (((2 * (warp & 3) + (lane >> 4)) ^ r) & 7) * 16, dzp[0], dzp[1], dzp[2],
+                dzp[3]);
+      }
+    }
+    if (dz_tma) {
+      fence_proxy_async();  // this thread's dz rows, before the store
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        tma_store_2d(&dzmap, static_cast<int>(col_base), static_cast<int>(tok0), z_s);
+        if (col_base + 64 < a.Dz) tma_store_2d(&dzmap, static_cast<int>(col_base) + 64, static_cast<int>(tok0), z_s + L::zbox);
+        bulk_commit();
+      }
     }
   }
+  if (threadIdx.x == 0) bulk_wait<0>();  // the last dz stores
   griddep_launch_dependents();  // only the dW partial store is left
   if (want_dw) {
     const int64_t grp = blockIdx.y;
@@ -496,8 +526,14 @@ int bwd_kt(RouterBwdArgs& a, const void* z, int64_t slices, int64_t groups, void
   rc = make_tmap_bf16_2d(&zmap, z, static_cast<uint64_t>(a.Dz), static_cast<uint64_t>(a.N),
                          static_cast<uint64_t>(a.Dz) * 2, 64, kBwdTile);
   if (rc != MOC_OK) return rc;
+  // dz: stored from the z area of the stage, kBwdTile rows at a time (a map of z, unused, when
+  // there is no dz or it is not 16-byte aligned)
+  CUtensorMap dzmap;
+  rc = make_tmap_bf16_2d(&dzmap, a.dz != nullptr && a.vec_dz ? static_cast<const void*>(a.dz) : z, static_cast<uint64_t>(a.Dz),
+                         static_cast<uint64_t>(a.N), static_cast<uint64_t>(a.Dz) * 2, 64, kBwdTile);
+  if (rc != MOC_OK) return rc;
   cudaError_t e = launch_pdl(k_router_bwd_tc<KT>, dim3(static_cast<unsigned>(slices), static_cast<unsigned>(groups)),
-                             dim3(256), BwdLayout<KT>::total, st, zmap, a);
+                             dim3(256), BwdLayout<KT>::total, st, zmap, dzmap, a);
   note_launch();
   if (e != cudaSuccess) return note_cuda(e);
   if (dw != nullptr) {
