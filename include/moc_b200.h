@@ -128,7 +128,8 @@ int moc_set_kernel_path(int path);
 int moc_forward(const moc_problem* p, const void* x, const void* alpha, const void* basis,
                 void* out, void* stream);
 
-/* Bytes of scratch memory moc_backward needs for problem p. */
+/* Bytes of scratch memory moc_backward needs for problem p.  The workspace passed to
+ * moc_backward must start on a 16-byte boundary (MOC_ERR_MISALIGNED otherwise). */
 size_t moc_backward_workspace_bytes(const moc_problem* p);
 
 /* Backward convolution.  dy is the gradient of out.  With activation = 1 the
@@ -158,7 +159,8 @@ int moc_router_forward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_t
                        int32_t router_act, const void* z, const void* weight, void* alpha,
                        void* stream);
 
-/* Bytes of scratch memory moc_router_backward needs. */
+/* Bytes of scratch memory moc_router_backward needs.  The workspace must start on a
+ * 16-byte boundary when dweight is requested (MOC_ERR_MISALIGNED otherwise). */
 size_t moc_router_backward_workspace_bytes(int64_t n_tokens, int64_t z_dim, int32_t n_bases,
                                            int32_t dtype);
 

@@ -459,6 +459,7 @@ __global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ C
 }
 
 // out[i] = sum over the groups' dW partials (fixed order), four lanes per element
+// (quad_part_sum): the sum is short (K x Dz elements) and spread over many partials
 __global__ void k_sum_groups(const float* __restrict__ part, int64_t groups, int64_t n, void* out, int dtype) {
   griddep_wait();  // the partials of the backward kernel
   const int sub = threadIdx.x & 3;
@@ -569,6 +570,7 @@ int tc_router_backward(int64_t N, int64_t Dz, int K, int act, const void* z, con
                        cudaStream_t st) {
   if (!aligned16(z) || !aligned16(w) || (dz && (reinterpret_cast<uintptr_t>(dz) & 3u))) return MOC_ERR_MISALIGNED;
   if (ws_bytes < tc_router_backward_ws(N, Dz, K)) return MOC_ERR_WORKSPACE_TOO_SMALL;
+  if (dw != nullptr && !aligned16(ws)) return MOC_ERR_MISALIGNED;  // partials are read 16 bytes at a time
   if (dz == nullptr && dw == nullptr) return MOC_OK;
   RouterBwdArgs a{};
   a.w = static_cast<const bf16*>(w);

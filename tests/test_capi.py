@@ -92,6 +92,16 @@ def test_workspace_query_needs_no_gpu():
     assert lib.moc_router_backward_workspace_bytes(16, 32, 4, 2) > 0
 
 
+def test_misaligned_workspace_rejected_before_any_launch():
+    """The backward kernels read their partial sums from the workspace 16 bytes at a time,
+    so a workspace that does not start on a 16-byte boundary is refused on the host
+    (MOC_ERR_MISALIGNED = 4), before any device call."""
+    lib = _lib.load()
+    p = _problem()
+    assert lib.moc_backward(ctypes.byref(p), 16, 16, 16, 16, 16, 16, 16, 4, 1 << 20, None) == 4
+    assert lib.moc_router_backward(16, 32, 8, 2, 0, 16, 16, 16, 16, 2, 16, 16, 8, 1 << 20, None) == 4
+
+
 def test_step_router_and_chunk_checks():
     lib = _lib.load()
     strides = (ctypes.c_int64 * 3)(32, 4, 1)
