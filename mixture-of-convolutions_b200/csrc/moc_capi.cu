@@ -181,7 +181,7 @@ int moc_backward(const moc_problem* p, const void* x, const void* alpha, const v
   if (rc != MOC_OK) return rc;
   if (!basis || !dbasis) return MOC_ERR_INVALID_ARGUMENT;
   if (p->n_tokens > 0 && (!x || !alpha || !dy || !dalpha)) return MOC_ERR_INVALID_ARGUMENT;
-  // the partial sums in the workspace are read 16 bytes at a time
+  // the tensor-core backward writes its dalpha partials 16 bytes at a time
   if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return MOC_ERR_MISALIGNED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (use_tc(*p)) {
@@ -360,7 +360,7 @@ int moc_router_backward(int64_t n_tokens, int64_t z_dim, int32_t n_bases, int32_
     return MOC_ERR_INVALID_ARGUMENT;
   if (n_bases > kMaxBasesSimt) return MOC_ERR_UNSUPPORTED_SHAPE;
   if (n_tokens > 0 && (!z || !weight || !alpha || !dalpha)) return MOC_ERR_INVALID_ARGUMENT;
-  // the dweight partials in the workspace are read 16 bytes at a time
+  // the workspace holds fp32 partials; 16-byte alignment, as for moc_backward's
   if (dweight != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return MOC_ERR_MISALIGNED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (g_kernel_path != MOC_PATH_GENERIC && tc_router_supported(n_tokens, z_dim, n_bases, dtype)) {

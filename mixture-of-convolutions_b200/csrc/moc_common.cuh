@@ -137,25 +137,6 @@ __device__ __forceinline__ float2 dsilu_bf2(float v0, float v1) {
 
 // ------------------------------------------------------------------ partial sums
 
-// Fixed-order sums of the `parts` partial rows (row p at base + p * stride floats) at the four
-// elements 4 i4 .. 4 i4 + 3, with 16-byte loads: rows are added in the order 0, 1, ..., so each
-// element gets the bits a one-element loop would.  base and stride must be multiples of four floats.
-__device__ __forceinline__ float4 part_sum4(const float* __restrict__ base, int64_t parts, int64_t stride,
-                                            int64_t i4) {
-  const float4* p = reinterpret_cast<const float4*>(base) + i4;
-  const int64_t s4 = stride / 4;
-  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-  for (int64_t r = 0; r < parts; ++r) {
-    const float4 v = __ldg(p + r * s4);
-    s.x += v.x;
-    s.y += v.y;
-    s.z += v.z;
-    s.w += v.w;
-  }
-  return s;
-}
-
 // Fixed-order sum of the `parts` partial rows (row p at base + p * stride) at element i, by the
 // four lanes sub = 0..3 of a lane quad (lanes 4m .. 4m + 3, all with the same i): lane sub adds
 // rows sub, sub + 4, ... in order, then the quad's four sums meet in a fixed shuffle tree, so

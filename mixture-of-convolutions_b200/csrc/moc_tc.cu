@@ -732,24 +732,25 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       }
 }
 
-// dalpha[i] = sum over channel slices, dbasis[i] = sum over token groups (fixed order), four
-// consecutive elements per thread (nk and ksd are multiples of 8: K % 8 == 0 on this path).
+// dalpha[i] = sum over channel slices, dbasis[i] = sum over token groups (fixed order).
 __global__ void k_tc_finalize(const float* __restrict__ da_part, int64_t n_slices, int64_t nk, void* dalpha,
                               int adt, const float* __restrict__ db_part, int64_t groups, int64_t ksd, void* dbasis,
                               int bdt) {
   griddep_wait();  // the partials of the backward kernel
-  const int64_t nk4 = nk / 4, total4 = nk4 + ksd / 4;
-  for (int64_t i4 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i4 < total4;
-       i4 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const bool da = i4 < nk4;
-    const float4 s = da ? part_sum4(da_part, n_slices, nk, i4) : part_sum4(db_part, groups, ksd, i4 - nk4);
-    void* out = da ? dalpha : dbasis;
-    const int dt = da ? adt : bdt;
-    const int64_t e = 4 * (da ? i4 : i4 - nk4);
-    st_any(out, dt, e, s.x);
-    st_any(out, dt, e + 1, s.y);
-    st_any(out, dt, e + 2, s.z);
-    st_any(out, dt, e + 3, s.w);
+  const int64_t total = nk + ksd;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float s = 0.f;
+    if (i < nk) {
+#pragma unroll 8
+      for (int64_t c = 0; c < n_slices; ++c) s += __ldg(da_part + c * nk + i);
+      st_any(dalpha, adt, i, s);
+    } else {
+      const int64_t j = i - nk;
+#pragma unroll 8
+      for (int64_t g = 0; g < groups; ++g) s += __ldg(db_part + g * ksd + j);
+      st_any(dbasis, bdt, j, s);
+    }
   }
   griddep_launch_dependents();
 }
@@ -931,7 +932,7 @@ void ws_split(const moc_problem& p, int64_t& slices, int64_t& groups, size_t& da
 
 int tc_finalize(const float* da_part, int64_t n_slices, int64_t nk, void* dalpha, int adt, const float* db_part,
                 int64_t groups, int64_t ksd, void* dbasis, int bdt, cudaStream_t st) {
-  const int64_t blocks = std::min<int64_t>(ceil_div((nk + ksd) / 4, 256), 8 * sm_count());
+  const int64_t blocks = std::min<int64_t>(ceil_div(nk + ksd, 256), 8 * sm_count());
   const cudaError_t e = launch_pdl(k_tc_finalize, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, da_part,
                                    n_slices, nk, dalpha, adt, db_part, groups, ksd, dbasis, bdt);
   note_launch();
@@ -978,7 +979,7 @@ size_t tc_backward_ws(const moc_problem& p) {
 
 int tc_backward(const moc_problem& p, const void* x, const void* alpha, const void* basis, const void* dy, void* dx,
                 void* dalpha, void* dbasis, void* ws, size_t ws_bytes, cudaStream_t st) {
-  if (!aligned16(ws)) return MOC_ERR_MISALIGNED;  // the partial sums are read 16 bytes at a time
+  if (!aligned16(ws)) return MOC_ERR_MISALIGNED;  // the dalpha partials are written 16 bytes at a time
   if (use_bwd5(p)) return tc5_backward(p, x, alpha, basis, dy, dx, dalpha, dbasis, ws, ws_bytes, st);
   if (!aligned16(x) || !aligned16(alpha) || !aligned16(basis) || !aligned16(dy) || (dx && !aligned16(dx)))
     return MOC_ERR_MISALIGNED;

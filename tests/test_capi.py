@@ -93,7 +93,7 @@ def test_workspace_query_needs_no_gpu():
 
 
 def test_misaligned_workspace_rejected_before_any_launch():
-    """The backward kernels read their partial sums from the workspace 16 bytes at a time,
+    """The conv backward writes its dalpha partials to the workspace 16 bytes at a time,
     so a workspace that does not start on a 16-byte boundary is refused on the host
     (MOC_ERR_MISALIGNED = 4), before any device call."""
     lib = _lib.load()
