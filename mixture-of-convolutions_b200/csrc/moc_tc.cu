@@ -40,6 +40,63 @@ constexpr int kFut = 16;               // future rows kept after each tile (S - 
 
 constexpr int align1k(int v) { return (v + 1023) / 1024 * 1024; }
 
+// ---- TMEM as the home of the backward's dbasis accumulators.  Each warp owns 8 S KT fp32
+// columns of its 32-lane quarter; a tap's 8 KT values per lane are loaded, advanced by
+// mma.sync and stored back once per 16-token block, so they take registers only while used.
+
+__device__ __forceinline__ void tm_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tm_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+// one warp: allocate ncols columns (address written to shared memory at slot)
+__device__ __forceinline__ void tm_alloc(uint32_t slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(slot), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tm_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tm_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void tm_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+// 8 consecutive fp32 columns of this thread's lane <-> v[0..1][0..3]
+__device__ __forceinline__ void tm_ld8(uint32_t taddr, float (&v)[2][4]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i >> 2][i & 3] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tm_st8(uint32_t taddr, const float (&v)[2][4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr),
+               "r"(__float_as_uint(v[0][0])), "r"(__float_as_uint(v[0][1])), "r"(__float_as_uint(v[0][2])),
+               "r"(__float_as_uint(v[0][3])), "r"(__float_as_uint(v[1][0])), "r"(__float_as_uint(v[1][1])),
+               "r"(__float_as_uint(v[1][2])), "r"(__float_as_uint(v[1][3]))
+               : "memory");
+}
+// a tap's 2 KT n-tiles of accumulators (8 KT columns); element copies, so v stays in registers
+template <int KT>
+__device__ __forceinline__ void tm_ld_tap(uint32_t taddr, float (&v)[2 * KT][4]) {
+#pragma unroll
+  for (int h = 0; h < KT; ++h) {
+    float t[2][4];
+    tm_ld8(taddr + 8 * h, t);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[2 * h + (i >> 2)][i & 3] = t[i >> 2][i & 3];
+  }
+}
+template <int KT>
+__device__ __forceinline__ void tm_st_tap(uint32_t taddr, const float (&v)[2 * KT][4]) {
+#pragma unroll
+  for (int h = 0; h < KT; ++h) {
+    float t[2][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t[i >> 2][i & 3] = v[2 * h + (i >> 2)][i & 3];
+    tm_st8(taddr + 8 * h, t);
+  }
+}
+constexpr int pow2_at_least(int v, int p = 32) { return p >= v ? p : pow2_at_least(v, 2 * p); }
+
 // PART (backward only) selects the work of one launch: kBwdAll (dx, dalpha and dbasis in
 // one pass), or, where the dbasis accumulators (S x KP x 16 channels per warp) would leave
 // no registers for anything else, two passes: kBwdDxDa (dx, dalpha) and kBwdDb (dbasis).
@@ -413,6 +470,12 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
   constexpr bool BREG = L::BREG;
   constexpr bool DXDA = PART != kBwdDb;  // this launch computes dx and dalpha
   constexpr bool DB = PART != kBwdDxDa;  // this launch computes dbasis
+  // dbasis accumulators live in TMEM (8 S KT columns per warp, two warps per lane quarter)
+  constexpr int kTmWarpCols = 8 * S * KT;
+  constexpr int kTmCols = pow2_at_least(2 * kTmWarpCols);
+  // one base group and at most 4 taps: the per-tap ldmatrix offsets are kept per lane and the
+  // four 16-token blocks of an item are unrolled (the registers the TMEM accumulators free)
+  constexpr bool kLean = KT == 1 && S <= 4;
   extern __shared__ __align__(1024) char smem_raw[];
   const Smem<L> sm(smem_raw);
   char* basis_s = sm.head;
@@ -437,8 +500,23 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
   const uint32_t x_box = static_cast<uint32_t>((warp >> 2) * L::xbox);
   const uint32_t dy_box = static_cast<uint32_t>(L::x_bytes + (warp >> 2) * L::dybox);
   const int m_chunk = 2 * (warp & 3) + (lane >> 4);
+  // per-tap lane offsets (a 16-row block step adds 2048 bytes and leaves the swizzle term alone):
+  // dz rows t + j, x rows kHalo + t - j, alpha rows t + j (dx) and t (the SiLU pre-activation)
+  uint32_t dyo[kLean ? S : 1], xo[kLean ? S : 1], ao[kLean ? S : 1], a0o = 0;
+  if constexpr (kLean) {
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      const int j = S - 1 - s, rd = j + lrow, rx = kHalo - j + lrow;
+      dyo[s] = dy_box + static_cast<uint32_t>(rd * 128 + (((m_chunk ^ rd) & 7) << 4));
+      xo[s] = x_box + static_cast<uint32_t>(rx * 128 + (((m_chunk ^ rx) & 7) << 4));
+      ao[s] = alpha_off<L>(j + lrow, lane >> 4);
+    }
+    a0o = alpha_off<L>(lrow, lane >> 4);
+  }
+  uint32_t tcol = 0;  // this warp's first TMEM accumulator column
+  // shared-memory word that receives the TMEM address (beside the mbarriers)
+  auto tm_slot = [&]() { return reinterpret_cast<uint32_t*>(sm.ost + L::ost_bytes + 16); };
 
-  float dba[DB ? S : 1][2 * KT][4] = {};  // dbasis^T accumulators: (ch g | g+8) x (k 8kn + 2q..)
   uint32_t bw[BREG ? S : 1][KT][4];  // basis, B operand of W = alpha . basis_s
   uint32_t bd[BREG ? S : 1][KT][4];  // basis^T, B operand of dalpha = m . basis_s^T
 
@@ -453,8 +531,22 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
     }
     load_basis<L, true>(a, basis_s, ch_base, S);
     cp_async_commit();
+    if constexpr (DB) {
+      if (warp == 0) {
+        tm_alloc(smem_addr(tm_slot()), kTmCols);
+        tm_fence_before();
+      }
+    }
     griddep_wait();  // x, dy and alpha may come from the kernels before this one
     __syncthreads();
+    if constexpr (DB) {
+      tm_fence_after();
+      tcol = *reinterpret_cast<volatile uint32_t*>(tm_slot()) + (static_cast<uint32_t>(32 * (warp & 3)) << 16) +
+             static_cast<uint32_t>((warp >> 2) * kTmWarpCols);
+      const float zero[2 * KT][4] = {};
+#pragma unroll
+      for (int s = 0; s < S; ++s) tm_st_tap<KT>(tcol + 8 * KT * s, zero);
+    }
     if (threadIdx.x == 0) {
       int64_t ss, se, r0, r1;
       if (a.rm.item(i0, ss, se, r0, r1))
@@ -474,6 +566,15 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
         atomicOr(&g_conv_status, kStatusWaitTimeout);
         mbar_wait(sm.bar + 8 * cur, parity);
         bulk_wait<0>();
+      }
+      if constexpr (DB) {  // the accumulators are given back before the CTA leaves
+        tm_wait_st();
+        tm_fence_before();
+        __syncthreads();
+        if (warp == 0) {
+          tm_fence_after();
+          tm_dealloc(*reinterpret_cast<volatile uint32_t*>(tm_slot()), kTmCols);
+        }
       }
       return;
     }
@@ -535,11 +636,14 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       return x_s + dy_box + r * 128 + (((m_chunk ^ r) & 7) << 4);
     };
     // W fragments (C layout) for alpha rows starting at tile row ar, tap s.
-    auto w_frag = [&](int ar, int s, float (&w)[2][4]) {
+    auto w_frag = [&](int ar, int s, float (&w)[2][4], uint32_t lean_off) {
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt) {
         uint32_t af[4];
-        ldsm_x4(a_s + (ar & ~15) * L::ARB + alpha_off<L>((ar & 15) + lrow, 2 * kt + (lane >> 4)), af);
+        if constexpr (kLean)  // KT == 1: lean_off is the lane's offset of rows (ar & 15) + lrow
+          ldsm_x4(a_s + (ar & ~15) * L::ARB + lean_off, af);
+        else
+          ldsm_x4(a_s + (ar & ~15) * L::ARB + alpha_off<L>((ar & 15) + lrow, 2 * kt + (lane >> 4)), af);
         uint32_t b0, b1, b2, b3;
         if constexpr (BREG) {
           b0 = bw[s][kt][0], b1 = bw[s][kt][1], b2 = bw[s][kt][2], b3 = bw[s][kt][3];
@@ -570,9 +674,12 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
             for (int s = 0; s < S; ++s) {
               const int j = S - 1 - s;
               float w[2][4];
-              w_frag(16 * b, s, w);
+              w_frag(16 * b, s, w, a0o);
               uint32_t xr[4];
-              ldsm_x4(x_addr(kHalo + 16 * b - j), xr);
+              if constexpr (kLean)
+                ldsm_x4(x_s + xo[s] + b * 2048, xr);
+              else
+                ldsm_x4(x_addr(kHalo + 16 * b - j), xr);
 #pragma unroll
               for (int nt = 0; nt < 2; ++nt) {
                 ffma2(pre[nt][0], pre[nt][1], w[nt][0], w[nt][1], bf_lo(xr[2 * nt]), bf_hi(xr[2 * nt]));
@@ -598,8 +705,8 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
 
     // ---- phase 2: per 16-row block: dx, m = dz * x_shift, dalpha, dbasis
     const int nb = (rows + 15) >> 4;  // uniform across the CTA
-#pragma unroll 1
-    for (int b = 0; b < nb; ++b) {
+    // one 16-token block of the item (b < nb)
+    auto block = [&](const int b) {
       uint32_t ab[DB ? KT : 1][4];  // alpha as the B operand of dbasis (tokens x bases)
       if constexpr (DB) {
 #pragma unroll
@@ -608,6 +715,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       }
       uint32_t dyu[4];  // dz (= dy without SiLU) of this block, packed bf16 pairs
       ldsm_x4(dy_addr(16 * b), dyu);
+      if constexpr (DB) tm_wait_st();  // the previous block's accumulator stores
       float dxa[2][4] = {};
       float daa[2 * KT][4] = {};
 #pragma unroll
@@ -615,9 +723,12 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
         const int j = S - 1 - s;
         if (want_dx) {
           float w[2][4];
-          w_frag(16 * b + j, s, w);  // W at rows t + j
+          w_frag(16 * b + j, s, w, kLean ? ao[s] : 0u);  // W at rows t + j
           uint32_t dys[4];
-          ldsm_x4(dy_addr(16 * b + j), dys);
+          if constexpr (kLean)
+            ldsm_x4(x_s + dyo[s] + b * 2048, dys);
+          else
+            ldsm_x4(dy_addr(16 * b + j), dys);
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
             ffma2(dxa[nt][0], dxa[nt][1], w[nt][0], w[nt][1], bf_lo(dys[2 * nt]), bf_hi(dys[2 * nt]));
@@ -625,7 +736,10 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
           }
         }
         uint32_t xr[4];
-        ldsm_x4(x_addr(kHalo + 16 * b - j), xr);
+        if constexpr (kLean)
+          ldsm_x4(x_s + xo[s] + b * 2048, xr);
+        else
+          ldsm_x4(x_addr(kHalo + 16 * b - j), xr);
         uint32_t m[4];  // A operand (tokens x channels) of dalpha, rounded to bf16
 #pragma unroll
         for (int r = 0; r < 4; ++r) m[r] = hmul2_bf16(dyu[r], xr[r]);
@@ -644,12 +758,16 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
           }
         }
         if constexpr (DB) {
+          float acc[2 * KT][4];  // this tap's dbasis^T accumulators, from TMEM
+          tm_ld_tap<KT>(tcol + 8 * KT * s, acc);
           uint32_t mt[4] = {movm_t(m[0]), movm_t(m[2]), movm_t(m[1]), movm_t(m[3])};
+          tm_wait_ld();
 #pragma unroll
           for (int kt = 0; kt < KT; ++kt) {
-            mma_bf16(dba[s][2 * kt], mt, ab[kt][0], ab[kt][1]);
-            mma_bf16(dba[s][2 * kt + 1], mt, ab[kt][2], ab[kt][3]);
+            mma_bf16(acc[2 * kt], mt, ab[kt][0], ab[kt][1]);
+            mma_bf16(acc[2 * kt + 1], mt, ab[kt][2], ab[kt][3]);
           }
+          tm_st_tap<KT>(tcol + 8 * KT * s, acc);
         }
       }
       if (dx_tma) {
@@ -671,7 +789,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       }
       // dalpha partial of this warp's 16 channels -> red_s[b % RB][warp]; the CTA adds the
       // 8 warps once every RB blocks (and after the tile's last block)
-      if constexpr (!DXDA) continue;
+      if constexpr (!DXDA) return;
       float* red = red_s + ((b % L::RB) * 8 + warp) * 16 * KP;
 #pragma unroll
       for (int kn = 0; kn < 2 * KT; ++kn)
@@ -711,6 +829,14 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
         }
         if (b < nb - 1) __syncthreads();  // red_s is rewritten by the next blocks of this tile
       }
+    };
+    if constexpr (kLean) {  // the four blocks unrolled
+#pragma unroll
+      for (int b = 0; b < kTile / 16; ++b)
+        if (b < nb) block(b);
+    } else {
+#pragma unroll 1
+      for (int b = 0; b < nb; ++b) block(b);
     }
     // the next iteration's wait barrier orders these reads of red_s and the stage before reuse
   }
@@ -719,6 +845,19 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
   griddep_launch_dependents();  // only the dbasis partial store is left
   // dbasis partial of this CTA: db_part[group][k][s][ch]
   if constexpr (!DB) return;
+  float dba[DB ? S : 1][2 * KT][4] = {};  // dbasis^T: (ch g | g+8) x (k 8kn + 2q..), from TMEM
+  if (i0 < i1) {
+    tm_wait_st();
+#pragma unroll
+    for (int s = 0; s < S; ++s) tm_ld_tap<KT>(tcol + 8 * KT * s, dba[s]);
+    tm_wait_ld();
+    tm_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+      tm_fence_after();
+      tm_dealloc(*reinterpret_cast<volatile uint32_t*>(tm_slot()), kTmCols);
+    }
+  }
   const int64_t grp = blockIdx.y;
 #pragma unroll
   for (int s = 0; s < (DB ? S : 1); ++s)
