@@ -130,23 +130,31 @@ __global__ void __launch_bounds__(kCommThreads) k_allreduce(const __grid_constan
     }
   }
   __syncthreads();
-  // 4. the rank-ordered sum of every rank's slice, a batch of peer loads in flight at once
+  // 4. the rank-ordered sum of every rank's slice: the batch's loads from all ranks are in
+  // flight at once (one NVLink round trip, not one per rank), then added in rank order
   if (ok) {
     for (int64_t i = i0 + threadIdx.x; i < i1; i += kBatch * kCommThreads) {
+      float t[MOC_COMM_MAX_RANKS][kBatch];
+#pragma unroll
+      for (int r = 0; r < MOC_COMM_MAX_RANKS; ++r) {
+        if (r < a.world) {
+          const float* src = a.bufs[r] + half;
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            const int64_t e = i + u * kCommThreads;
+            t[r][u] = e < i1 ? __ldcg(src + e) : 0.f;  // L2 / peer, never a stale L1 line
+          }
+        }
+      }
       float v[kBatch];
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) v[u] = 0.f;
-      for (int r = 0; r < a.world; ++r) {
-        const float* src = a.bufs[r] + half;
-        float t[kBatch];
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-          const int64_t e = i + u * kCommThreads;
-          t[u] = e < i1 ? __ldcg(src + e) : 0.f;  // L2 / peer, never a stale L1 line
+      for (int r = 0; r < MOC_COMM_MAX_RANKS; ++r)
+        if (r < a.world) {
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) v[u] += t[r][u];
         }
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) v[u] += t[u];
-      }
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
         const int64_t e = i + u * kCommThreads;
