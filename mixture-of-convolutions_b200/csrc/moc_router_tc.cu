@@ -207,9 +207,10 @@ struct RouterBwdArgs {
 
 // TMA-staged backward: thread 0 double-buffers 64-token x 128-column z tiles (two
 // 128B-swizzled boxes) on mbarriers; every thread computes dlogits for the next tile's
-// tokens meanwhile.
+// tokens meanwhile.  At most 72 registers for two base groups: three CTAs per SM, so that the
+// grid (sized for 3 per SM) is one wave.
 template <int KT>
-__global__ void __launch_bounds__(256) k_router_bwd_tc(const __grid_constant__ CUtensorMap zmap,
+__global__ void __launch_bounds__(256, (KT == 1 ? 4 : 3)) k_router_bwd_tc(const __grid_constant__ CUtensorMap zmap,
                                                       const __grid_constant__ CUtensorMap dzmap, RouterBwdArgs a) {
   using L = BwdLayout<KT>;
   constexpr int KP = L::KP;
@@ -494,6 +495,10 @@ int set_smem(const void* kern, bool (&configured)[64], int smem) {
   if (e != cudaSuccess) return note_cuda(e);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    // the whole unified L1 / shared array as shared memory, so that as many CTAs as the
+    // registers allow are resident (these kernels stage through shared memory, not L1)
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return note_cuda(e);
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
