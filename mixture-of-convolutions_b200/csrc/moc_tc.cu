@@ -132,10 +132,11 @@ struct Layout {
   static constexpr int red_bytes = (BWD && PART != kBwdDb) ? RB * 8 * 16 * KP * 4 : 0;
   // with register-resident basis fragments the basis staging area is reused for the
   // dalpha reduction buffer once the fragments are loaded
-  // the forward at 32 bases and more than 4 taps stages its basis (up to 68 KB) through the
-  // stage buffers, a few taps per pass, before the first tile is loaded: its fragments live
-  // in registers afterwards, and two CTAs then fit an SM
-  static constexpr bool BALIAS = !BWD && KT * S > 8;
+  // the forward stages its basis through the stage buffers, a few taps per pass, before the
+  // first tile is loaded, and keeps its fragments in registers afterwards: at 32 bases and more
+  // than 4 taps (up to 68 KB) so that two CTAs fit an SM, at one base group and up to 4 taps
+  // so that four fit (45 KB and 64 registers each)
+  static constexpr bool BALIAS = !BWD && (KT * S > 8 || (KT == 1 && S <= 4));
   static constexpr int head_bytes =
       BALIAS ? 0
              : align1k((BWD && BREG) ? (basis_bytes > red_bytes ? basis_bytes : red_bytes) : basis_bytes + red_bytes);
@@ -143,7 +144,7 @@ struct Layout {
   static constexpr int ost_bytes = BWD ? 0 : 8 * 16 * 32;
   // (the SiLU backward needs no staging of its own: it writes dz, bf16, over dy in the tile)
   static constexpr int total = 1024 + 2 * stage_bytes + head_bytes + ost_bytes + 64;
-  static constexpr int min_blocks = BWD ? ((BREG && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 3 : 2);
+  static constexpr int min_blocks = BWD ? ((BREG && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 4 : 2);
 };
 
 struct TcArgs {
