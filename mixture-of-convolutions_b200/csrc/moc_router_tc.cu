@@ -478,10 +478,12 @@ int sm_count_r() {
   return n > 0 ? n : 148;
 }
 
-void bwd_plan(int64_t N, int64_t Dz, int64_t& slices, int64_t& groups, int64_t& tpg) {
+// Grid of the backward: slices x token groups, one wave of the CTAs an SM holds (four at one
+// base group, three at two: the kernel's launch bounds).
+void bwd_plan(int64_t N, int64_t Dz, int K, int64_t& slices, int64_t& groups, int64_t& tpg) {
   slices = ceil_div(Dz, kZC);
   const int64_t tiles = std::max<int64_t>(1, ceil_div(N, kBwdTile));
-  const int64_t target = static_cast<int64_t>(sm_count_r()) * 3;
+  const int64_t target = static_cast<int64_t>(sm_count_r()) * (K <= 16 ? 4 : 3);
   groups = std::min<int64_t>(tiles, std::max<int64_t>(1, target / slices));
   tpg = ceil_div(tiles, groups);
   groups = ceil_div(tiles, tpg);
@@ -566,7 +568,7 @@ int tc_router_forward(int64_t N, int64_t Dz, int K, int act, const void* z, cons
 
 size_t tc_router_backward_ws(int64_t N, int64_t Dz, int K) {
   int64_t slices, groups, tpg;
-  bwd_plan(N, Dz, slices, groups, tpg);
+  bwd_plan(N, Dz, K, slices, groups, tpg);
   return align_up(static_cast<size_t>(groups * K * Dz) * sizeof(float), 256);
 }
 
@@ -590,7 +592,7 @@ int tc_router_backward(int64_t N, int64_t Dz, int K, int act, const void* z, con
   a.vec_ad = da_dtype == MOC_DTYPE_BF16 && aligned16(alpha) && aligned16(dalpha) && K % 8 == 0;
   a.vec_dz = dz != nullptr && aligned16(dz);
   int64_t slices, groups, tpg;
-  bwd_plan(N, Dz, slices, groups, tpg);
+  bwd_plan(N, Dz, K, slices, groups, tpg);
   a.tiles_per_group = tpg;
   return K <= 16 ? bwd_kt<1>(a, z, slices, groups, dw, st) : bwd_kt<2>(a, z, slices, groups, dw, st);
 }
