@@ -18,6 +18,9 @@
 //   backward: dz (SiLU pre recomputed on chip), dx, per-slice dalpha partials and per-CTA
 //             dbasis partials in one pass over x, dy, alpha; a second small kernel adds the
 //             partials in a fixed order (deterministic, no atomics).
+// y and dx leave through the stage they were computed from (each 16-row block overwrites
+// rows no later block reads) by TMA stores, one per 64-channel box and tile.  Between blocks
+// the backward keeps its dbasis accumulators in tensor memory (tcgen05.ld / st per tap).
 #include <algorithm>
 
 #include "moc_common.cuh"
