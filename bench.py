@@ -651,6 +651,84 @@ def run_reference(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_triton_reference(args) -> None:
+    """The reference's own GPU path (its Triton kernels, the unmodified package installed in
+    baseline/_ref) at config 2 on one GPU, beside this library's figures in profiles/: each
+    operation and the module step as CUDA-graph replays timed with CUDA events.  Imports the
+    reference's `moc` instead of this library's, so it runs alone in its process."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "moc")):
+        print(json.dumps({"impl": "reference-triton", "unavailable": "the reference is not installed in baseline/_ref"}))
+        return
+    sys.path.insert(0, ref_dir)
+    import moc as rmoc  # noqa: E402  (the reference package)
+    from moc import ops as rops  # noqa: E402
+
+    if not rmoc.__file__.startswith(ref_dir):
+        raise RuntimeError(f"expected the reference package, imported {rmoc.__file__}")
+    dev = torch.device("cuda", 0)
+    side = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(side)  # every launch, warm-up included, on one non-default stream
+    B, T, D, Dz, K, S = CONFIG["B"], CONFIG["T"], CONFIG["D"], CONFIG["Dz"], CONFIG["K"], CONFIG["S"]
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(B, T, D, generator=g).bfloat16().to(dev)
+    z = torch.randn(B, T, Dz, generator=g).bfloat16().to(dev)
+    dy = torch.randn(B, T, D, generator=g).bfloat16().to(dev)
+    m = rmoc.MoC(dim=D, z_dim=Dz, kernel_size=S, k=K, init_std=0.002, router_activation="softmax")
+    with torch.no_grad():
+        m.router.normal_(0, 0.02)
+    m = m.to(device=dev, dtype=torch.bfloat16)
+    with torch.no_grad():
+        alpha = torch.softmax(torch.nn.functional.linear(z, m.router), -1)
+    basis = m.conv_bases.detach()
+
+    def gtime(fn, reps=20):
+        fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            for _ in range(reps):
+                fn()
+        gr.replay()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(side)
+        for _ in range(3):
+            gr.replay()
+        s1.record(side)
+        torch.cuda.synchronize()
+        return s0.elapsed_time(s1) / (3 * reps)
+
+    xx, zz = x.clone().requires_grad_(), z.clone().requires_grad_()
+
+    def step():
+        y, _ = m(xx, zz)
+        torch.autograd.grad(y, (xx, zz, m.conv_bases, m.router), dy)
+
+    zr, wr = z.clone().requires_grad_(), m.router.detach().clone().requires_grad_()
+
+    def router_fb():
+        a = torch.softmax(torch.nn.functional.linear(zr, wr), -1)
+        torch.autograd.grad(a, (zr, wr), alpha)
+
+    t0 = time.time()
+    for _ in range(2):  # the Triton autotuners run here
+        step()
+    torch.cuda.synchronize()
+    res = {"impl": "reference-triton", "config": "config2: B=4 T=4096 D=z_dim=2048 K=16 S=4 bf16 softmax",
+           "warmup_autotune_s": time.time() - t0, "triton": __import__("triton").__version__,
+           "gpu": torch.cuda.get_device_name(0)}
+    res["conv_forward_ms"] = gtime(lambda: rops.launch_forward(x, alpha, basis, activation_flag=0))
+    res["conv_backward_ms"] = gtime(lambda: rops.launch_backward(x, alpha, basis, dy, dy, activation_flag=0,
+                                                                  need_x=True))
+    with torch.no_grad():
+        res["router_forward_ms"] = gtime(lambda: torch.softmax(torch.nn.functional.linear(z, m.router), -1))
+    res["router_fwd_bwd_ms"] = gtime(router_fb)
+    res["module_step_ms"] = gtime(step, reps=10)
+    res["tokens_per_s"] = B * T / (res["module_step_ms"] * 1e-3)
+    print(json.dumps(res), flush=True)
+
+
 # ----------------------------------------------------------------------------- main
 
 def main() -> None:
@@ -659,6 +737,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--triton-reference", action="store_true",
+                    help="time the reference's own Triton GPU path (baseline/_ref) at config 2 and exit")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra-workloads", action="store_true",
                     help="with the default workload on one GPU, skip the short varlen / decode / large runs "
@@ -673,6 +753,9 @@ def main() -> None:
                          "convolution forward of q/k/v modules (prefill)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.triton_reference:
+        run_triton_reference(args)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
