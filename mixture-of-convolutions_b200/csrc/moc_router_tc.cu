@@ -271,14 +271,17 @@ __global__ void __launch_bounds__(256, (KT == 1 ? 4 : 3)) k_router_bwd_tc(const 
   }
   if (i0 >= i1) griddep_wait();  // a CTA without tiles still writes its (zero) dW partial
   // alpha / dalpha of the next tile are loaded one iteration ahead into registers: four
-  // threads per token, each owning KP/4 bases
+  // threads per token, each owning KP/4 bases.  The bf16 pairs stay packed until the next
+  // iteration uses them, so nothing waits on the loads before then.
   constexpr int KQ = KP / 4;
   const int dl_row = threadIdx.x >> 2, dl_part = threadIdx.x & 3;
-  float av[KQ], dv[KQ];
+  float av[KQ], dv[KQ];               // the element path: values
+  uint32_t wa[KQ / 2], wd[KQ / 2];    // the vector path: packed bf16 pairs
   auto fetch = [&](int64_t tile) {
     const int64_t tok = tile * kBwdTile + dl_row;
     if (a.vec_ad) {  // K % 8 == 0: a thread's KQ bases are all valid or all padding
-      uint32_t wa[KQ / 2] = {}, wd[KQ / 2] = {};
+#pragma unroll
+      for (int e = 0; e < KQ / 2; ++e) wa[e] = 0u, wd[e] = 0u;
       if (tok < a.N && dl_part * KQ < a.K) {
         const bf16* pa = a.alpha + tok * a.K + dl_part * KQ;
         const bf16* pd = static_cast<const bf16*>(a.dalpha) + tok * a.K + dl_part * KQ;
@@ -294,11 +297,6 @@ __global__ void __launch_bounds__(256, (KT == 1 ? 4 : 3)) k_router_bwd_tc(const 
             wd[4 * v] = vd.x, wd[4 * v + 1] = vd.y, wd[4 * v + 2] = vd.z, wd[4 * v + 3] = vd.w;
           }
         }
-      }
-#pragma unroll
-      for (int e = 0; e < KQ / 2; ++e) {
-        av[2 * e] = bf_lo(wa[e]), av[2 * e + 1] = bf_hi(wa[e]);
-        dv[2 * e] = bf_lo(wd[e]), dv[2 * e + 1] = bf_hi(wd[e]);
       }
       return;
     }
@@ -319,6 +317,13 @@ __global__ void __launch_bounds__(256, (KT == 1 ? 4 : 3)) k_router_bwd_tc(const 
     // dlogits for this tile's 64 tokens (bf16, like the reference's bf16 autograd); the
     // softmax dot is a quad reduction.
     {
+      if (a.vec_ad) {
+#pragma unroll
+        for (int e = 0; e < KQ / 2; ++e) {
+          av[2 * e] = bf_lo(wa[e]), av[2 * e + 1] = bf_hi(wa[e]);
+          dv[2 * e] = bf_lo(wd[e]), dv[2 * e + 1] = bf_hi(wd[e]);
+        }
+      }
       float dot = 0.f;
 #pragma unroll
       for (int e = 0; e < KQ; ++e) dot = fmaf(av[e], dv[e], dot);
