@@ -540,8 +540,13 @@ def run_proj(args, rank: int, world: int, local_rank: int) -> dict | None:
         offs.append(offs[-1] + D)
     w_rows = [w_qkv[offs[i]:offs[i + 1]] for i in range(len(mods))]
 
-    def step_fused():
-        return fused.proj_forward_multi(h, w_qkv, mods, z=h)
+    def step_fused():  # inference: no autograd graph, so the launch writes y only
+        with torch.no_grad():
+            return fused.proj_forward_multi(h, w_qkv, mods, z=h)
+
+    def q_only():
+        with torch.no_grad():
+            return fused.proj_forward(h, w_rows[0], mods[0], alpha=alpha_q)
 
     def step_unfused():
         with torch.no_grad():
@@ -576,9 +581,30 @@ def run_proj(args, rank: int, world: int, local_rank: int) -> dict | None:
     ms_unfused = graph_time(step_unfused, max(3, min(args.steps, 10)), device)
     # the fused kernel alone on the widest module (router output precomputed)
     alpha_q = ops.launch_router_forward(h, mods[0].router.detach(), mods[0].router_activation)
-    k_ms = graph_time(lambda: fused.proj_forward(h, w_rows[0], mods[0], alpha=alpha_q),
-                      max(3, min(args.steps, 10)), device)
+    k_ms = graph_time(q_only, max(3, min(args.steps, 10)), device)
     k_flops = 2.0 * B * T * Dm * mods[0].dim
+    # the training step of the same block: forward + backward of h, qkv_proj.weight and every
+    # module's conv_bases and router, fused (the launch keeps each module's x for the backward)
+    # against unfused (the projection GEMM writes qkv, each module reads its slice back)
+    hq = h.detach().clone().requires_grad_()
+    wq = w_qkv.detach().clone().requires_grad_()
+    params = [p for m in mods for p in (m.conv_bases, m.router)]
+    dys = [torch.randn(B, T, D, generator=g).bfloat16().to(device) for _, D, _ in c["modules"]]
+
+    def train_fused():
+        return torch.autograd.grad(fused.proj_forward_multi(hq, wq, mods, z=hq), [hq, wq] + params, grad_outputs=dys)
+
+    def train_unfused():
+        qkv = torch.matmul(hq, wq.T)
+        ys = [m(qkv[..., offs[i]:offs[i + 1]], hq)[0] for i, m in enumerate(mods)]
+        return torch.autograd.grad(ys, [hq, wq] + params, grad_outputs=dys)
+
+    for a_, b_ in zip(train_fused(), train_unfused()):
+        err = float((a_.float() - b_.float()).abs().max() / b_.float().abs().max().clamp_min(1e-30))
+        assert err <= 2e-2, f"fused and unfused training gradients differ: {err:.3e}"
+    reps = max(3, min(args.steps, 10))
+    ms_train = max_over_ranks(graph_time(train_fused, reps, device), world)
+    ms_train_unfused = max_over_ranks(graph_time(train_unfused, reps, device), world)
     peaks = measured_peaks()
     peak_tf = peaks.get("bf16_tflops", FALLBACK_BF16_TFLOPS)
     tokens = B * T
@@ -595,6 +621,11 @@ def run_proj(args, rank: int, world: int, local_rank: int) -> dict | None:
                                  "CUDA events"},
             "unfused_ms_per_step": ms_unfused,
             "unfused": "cuBLAS qkv GEMM (torch.matmul) + each module's router and MoC forward on its slice",
+            "train_ms_per_step": ms_train, "train_unfused_ms_per_step": ms_train_unfused,
+            "train": "forward + backward (gradients of h, qkv_proj.weight, each module's conv_bases and router): "
+                     "fused = one moc_proj_forward_multi_save launch keeping each module's x, then per module "
+                     "moc_backward and the router backward, then the dh / dweight GEMMs (cuBLAS) over the modules' "
+                     "dx; unfused = the same through the qkv GEMM and each module's autograd; CUDA graph, CUDA events",
             "roofline": {"bound": "tensor", "kernel": "k_proj_conv (q module, D=4096)", "achieved": k_flops / (k_ms * 1e-3) / 1e12,
                          "peak": peak_tf, "peak_source": "measured" if "bf16_tflops" in peaks else "fallback",
                          "unit": "TFLOP/s", "frac": k_flops / (k_ms * 1e-3) / 1e12 / peak_tf,
@@ -769,7 +800,7 @@ def main() -> None:
     if line is not None and args.workload == "train" and world == 1 and not args.no_extra_workloads:
         # the other BASELINE workloads, short runs on the same GPU, reported in the same line
         extra = {}
-        for name in ("varlen", "decode", "large"):
+        for name in ("varlen", "decode", "large", "proj"):
             sub = argparse.Namespace(**vars(args))
             sub.workload, sub.steps, sub.warmup, sub.batch = name, min(args.steps, 20), 3, None
             sub.no_cpu_baseline = True
@@ -783,7 +814,8 @@ def main() -> None:
 def summarize(line: dict) -> dict:
     """The keys of a workload's line that the headline line carries for it."""
     keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "higher_is_better", "config", "roofline",
-            "kernel_ms", "e2e", "per_module_path_us", "gpu_launches", "clocks", "step_hbm_frac")
+            "kernel_ms", "e2e", "per_module_path_us", "gpu_launches", "clocks", "step_hbm_frac",
+            "unfused_ms_per_step", "train_ms_per_step", "train_unfused_ms_per_step")
     return {k: line[k] for k in keep if k in line}
 
 

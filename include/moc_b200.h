@@ -258,11 +258,10 @@ int moc_decode_step_multi(int32_t n_modules, const moc_decode_module* modules, i
  * The projection feeding a MoC module (the q, k or v slice of the reference's qkv_proj,
  * README.md:115-129) runs on the tensor cores (tcgen05, accumulators in tensor memory) with
  * the convolution as its epilogue: the projected x is rounded to bf16 on chip, as the
- * reference's bf16 qkv tensor is, and never written to memory.  Forward only (inference and
- * prefill without a cache); training runs the projection and moc_forward / moc_backward
- * separately.  Requires n_bases % 8 == 0 and n_bases <= 16, 1 <= kernel_size <= 8,
- * in_dim % 8 == 0 and dim % 8 == 0.  Not in the reference, which applies MoC after a
- * separate projection GEMM. */
+ * reference's bf16 qkv tensor is, and never written to memory (inference and prefill
+ * without a cache; for training, moc_proj_forward_save below also writes it out).
+ * Requires n_bases % 8 == 0 and n_bases <= 16, 1 <= kernel_size <= 8, in_dim % 8 == 0 and
+ * dim % 8 == 0.  Not in the reference, which applies MoC after a separate projection GEMM. */
 typedef struct moc_proj_problem {
   int64_t batch, seq_len;
   int64_t in_dim, dim;
@@ -275,6 +274,15 @@ typedef struct moc_proj_problem {
   void* out;
 } moc_proj_problem;
 int moc_proj_forward(const moc_proj_problem* problem, void* stream);
+
+/* The training form of moc_proj_forward: the same out, and x_out [batch * seq_len, dim] (bf16,
+ * 16-byte aligned) receives the rounded projection x = h . weight^T that the convolution read.
+ * The backward is then the convolution's (moc_backward on x, alpha, basis and dy gives dx,
+ * dalpha, dbasis) followed by the projection's two GEMMs, dh = dx . weight and
+ * dweight = dx^T . h, which are plain library GEMMs (the caller's BLAS).  Against the unfused
+ * training forward (projection GEMM writing x, then moc_forward reading it back) this saves
+ * one read of x and one launch.  x_out NULL is moc_proj_forward. */
+int moc_proj_forward_save(const moc_proj_problem* problem, void* x_out, void* stream);
 
 /* Several modules over one projection, in one launch: the reference's
  *   q, k, v = qkv_proj(x_norm).split(...);  q = q_conv(q, x_norm); ...
@@ -294,6 +302,14 @@ typedef struct moc_proj_module {
 int moc_proj_forward_multi(int32_t n_modules, const moc_proj_module* modules, int64_t batch, int64_t seq_len,
                            int64_t in_dim, int32_t kernel_size, const void* h, const void* weight,
                            int64_t weight_rows, void* stream);
+
+/* The training form of moc_proj_forward_multi: x_out holds n_modules pointers, module i's
+ * rounded projection [batch * seq_len, dim_i] (bf16, 16-byte aligned; a NULL entry skips that
+ * module's copy).  x_out NULL is moc_proj_forward_multi.  The backward as for
+ * moc_proj_forward_save, with dweight's rows [row_offset, row_offset + dim) from module i. */
+int moc_proj_forward_multi_save(int32_t n_modules, const moc_proj_module* modules, void* const* x_out,
+                                int64_t batch, int64_t seq_len, int64_t in_dim, int32_t kernel_size, const void* h,
+                                const void* weight, int64_t weight_rows, void* stream);
 
 /* Gradient all-reduce over NVLink peer memory, for the data-parallel step (one process
  * per GPU).  The step's only collective sums the parameter gradients (conv_bases and

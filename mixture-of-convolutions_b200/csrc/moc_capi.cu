@@ -236,6 +236,13 @@ int moc_decode_step_multi(int32_t n_modules, const moc_decode_module* modules, i
 int moc_proj_forward_multi(int32_t n_modules, const moc_proj_module* modules, int64_t batch, int64_t seq_len,
                            int64_t in_dim, int32_t kernel_size, const void* h, const void* weight,
                            int64_t weight_rows, void* stream) {
+  return moc_proj_forward_multi_save(n_modules, modules, nullptr, batch, seq_len, in_dim, kernel_size, h, weight,
+                                     weight_rows, stream);
+}
+
+int moc_proj_forward_multi_save(int32_t n_modules, const moc_proj_module* modules, void* const* x_out,
+                                int64_t batch, int64_t seq_len, int64_t in_dim, int32_t kernel_size, const void* h,
+                                const void* weight, int64_t weight_rows, void* stream) {
   if (n_modules < 1 || n_modules > MOC_PROJ_MAX_MODULES || !modules) return MOC_ERR_INVALID_ARGUMENT;
   if (batch < 0 || seq_len < 0 || in_dim <= 0 || kernel_size <= 0 || weight_rows <= 0) return MOC_ERR_INVALID_ARGUMENT;
   if (kernel_size > 8 || in_dim % 8 != 0) return MOC_ERR_UNSUPPORTED_SHAPE;
@@ -253,16 +260,19 @@ int moc_proj_forward_multi(int32_t n_modules, const moc_proj_module* modules, in
     if (batch > 0 && seq_len > 0) {
       if (!m.alpha || !m.basis || !m.out) return MOC_ERR_INVALID_ARGUMENT;
       if (!a16(m.alpha) || !a16(m.basis) || !a16(m.out)) return MOC_ERR_MISALIGNED;
+      if (x_out && !a16(x_out[i])) return MOC_ERR_MISALIGNED;  // NULL (no copy) is aligned
     }
   }
   if (batch == 0 || seq_len == 0) return MOC_OK;
   if (!h || !weight) return MOC_ERR_INVALID_ARGUMENT;
   if (!a16(h) || !a16(weight)) return MOC_ERR_MISALIGNED;
-  return proj_forward_multi(n_modules, modules, batch, seq_len, in_dim, kernel_size, h, weight, weight_rows,
+  return proj_forward_multi(n_modules, modules, x_out, batch, seq_len, in_dim, kernel_size, h, weight, weight_rows,
                             static_cast<cudaStream_t>(stream));
 }
 
-int moc_proj_forward(const moc_proj_problem* p, void* stream) {
+int moc_proj_forward(const moc_proj_problem* p, void* stream) { return moc_proj_forward_save(p, nullptr, stream); }
+
+int moc_proj_forward_save(const moc_proj_problem* p, void* x_out, void* stream) {
   if (!p) return MOC_ERR_INVALID_ARGUMENT;
   if (p->dim <= 0) return MOC_ERR_INVALID_ARGUMENT;
   if (p->dim % 8 != 0) return MOC_ERR_UNSUPPORTED_SHAPE;
@@ -274,8 +284,9 @@ int moc_proj_forward(const moc_proj_problem* p, void* stream) {
   m.alpha = p->alpha;
   m.basis = p->basis;
   m.out = p->out;
-  return moc_proj_forward_multi(1, &m, p->batch, p->seq_len, p->in_dim, p->kernel_size, p->h, p->weight, p->dim,
-                                stream);
+  void* const xs[1] = {x_out};
+  return moc_proj_forward_multi_save(1, &m, xs, p->batch, p->seq_len, p->in_dim, p->kernel_size, p->h, p->weight,
+                                     p->dim, stream);
 }
 
 int moc_comm_create(int32_t rank, int32_t world, int64_t capacity, moc_comm** comm, void* handle_out) {

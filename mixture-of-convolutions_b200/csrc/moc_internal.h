@@ -68,9 +68,10 @@ int tc_router_backward_noalloc(int64_t N, int64_t Dz, int K, int act, const void
 // fused decode step of up to MOC_DECODE_MAX_MODULES modules sharing z (moc_decode.cu)
 int decode_step_multi(int n, const moc_decode_module* mods, int64_t B, int64_t Dz, const void* z, cudaStream_t st);
 
-// fused projection GEMM (tcgen05) + convolution forward (moc_proj.cu)
-int proj_forward_multi(int n, const moc_proj_module* mods, int64_t batch, int64_t seq_len, int64_t in_dim, int S,
-                       const void* h, const void* weight, int64_t weight_rows, cudaStream_t st);
+// fused projection GEMM (tcgen05) + convolution forward (moc_proj.cu); x_out (NULL, or one
+// pointer per module, each NULL or [batch * seq_len, dim]) receives the rounded projection
+int proj_forward_multi(int n, const moc_proj_module* mods, void* const* x_out, int64_t batch, int64_t seq_len,
+                       int64_t in_dim, int S, const void* h, const void* weight, int64_t weight_rows, cudaStream_t st);
 int proj_status(int* out, bool clear);
 
 // gradient all-reduce over NVLink peer memory (moc_comm.cu); CommImpl is the object

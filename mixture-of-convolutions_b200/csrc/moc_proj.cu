@@ -27,7 +27,9 @@
 //              round to bf16 into a swizzled x tile in shared memory (rows before the
 //              sequence start zeroed), release the accumulator, then convolve exactly as the
 //              standalone forward does (W_s = alpha . basis_s on mma.sync, FFMA2 taps, fused
-//              SiLU) and store y through per-warp staging rows with 16-byte stores.
+//              SiLU) and store y through per-warp staging rows with 16-byte stores.  For
+//              training the epilogue also copies the tile's rounded x rows to memory (the
+//              input of the convolution backward); inference writes y only.
 // The two accumulators let the MMAs of tile i+1 run under the epilogue of tile i; the
 // leader reuses an accumulator once both CTAs' epilogues have released it.
 //
@@ -88,6 +90,7 @@ struct ProjMod {
   const bf16* alpha;
   const bf16* basis;
   bf16* y;
+  bf16* x;          // optional: the rounded projection, kept for the backward
   int64_t dout;     // channels
   int64_t row_off;  // first weight row
   int64_t tile0;    // first channel tile (over all modules)
@@ -452,6 +455,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 #pragma unroll
         for (int s = 0; s < S; ++s)
           ldsm_x4_t(smem_addr(b_s + (s * kPKP + lrow) * kPRowB + (e * 16 + lcol) * 2), bw[s]);
+        if (md.x != nullptr) {
+          // training: the half's output rows of the rounded projection go to memory too, as
+          // the x the convolution backward reads (16-byte chunks, 16 per 128-channel row)
+          bf16* xg = md.x + c.m0 * md.dout + c0;
+          for (int idx = et; idx < c.rows * 16; idx += kPEpiThreads) {
+            const int r = idx >> 4, chunk = idx & 15;
+            if (c0 + chunk * 8 < md.dout) {
+              const int xr = kPHalo + r;
+              const uint4 v = *reinterpret_cast<const uint4*>(x_s + (chunk >> 3) * kPXBox + xr * 128 +
+                                                              (((chunk & 7) ^ (xr & 7)) << 4));
+              *reinterpret_cast<uint4*>(xg + static_cast<int64_t>(r) * md.dout + chunk * 8) = v;
+            }
+          }
+        }
         // ---- the convolution of the tile's output rows (x row = output row + halo)
         const int64_t ch_w = c0 + e * 16;
         bf16* out_tile = md.y + c.m0 * md.dout + ch_w;
@@ -540,8 +557,8 @@ int proj_inst(ProjArgs& args, const void* h, const void* weight, int64_t weight_
 
 }  // namespace
 
-int proj_forward_multi(int n, const moc_proj_module* mods, int64_t batch, int64_t seq_len, int64_t in_dim, int S,
-                       const void* h, const void* weight, int64_t weight_rows, cudaStream_t st) {
+int proj_forward_multi(int n, const moc_proj_module* mods, void* const* x_out, int64_t batch, int64_t seq_len,
+                       int64_t in_dim, int S, const void* h, const void* weight, int64_t weight_rows, cudaStream_t st) {
   ProjArgs a{};
   a.n_mod = n;
   a.seq_len = seq_len;
@@ -555,6 +572,7 @@ int proj_forward_multi(int n, const moc_proj_module* mods, int64_t batch, int64_
     m.alpha = static_cast<const bf16*>(mods[i].alpha);
     m.basis = static_cast<const bf16*>(mods[i].basis);
     m.y = static_cast<bf16*>(mods[i].out);
+    m.x = x_out ? static_cast<bf16*>(x_out[i]) : nullptr;
     m.dout = mods[i].dim;
     m.row_off = mods[i].row_offset;
     m.tile0 = tiles;

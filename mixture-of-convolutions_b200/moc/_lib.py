@@ -143,6 +143,9 @@ SIGNATURES = {
     "moc_proj_forward": (ctypes.c_int, [ctypes.POINTER(MocProjProblem), _P]),
     "moc_proj_forward_multi": (ctypes.c_int, [_I32, ctypes.POINTER(MocProjModule), _I64, _I64, _I64, _I32, _P, _P,
                                               _I64, _P]),
+    "moc_proj_forward_save": (ctypes.c_int, [ctypes.POINTER(MocProjProblem), _P, _P]),
+    "moc_proj_forward_multi_save": (ctypes.c_int, [_I32, ctypes.POINTER(MocProjModule), ctypes.POINTER(_P), _I64,
+                                                   _I64, _I64, _I32, _P, _P, _I64, _P]),
     "moc_comm_create": (ctypes.c_int, [_I32, _I32, _I64, ctypes.POINTER(_P), _P]),
     "moc_comm_connect": (ctypes.c_int, [_P, _P]),
     "moc_comm_allreduce": (ctypes.c_int, [_P, _I32, ctypes.POINTER(_P), ctypes.POINTER(_I64), ctypes.POINTER(_I32), _P]),

@@ -202,11 +202,14 @@ class _RouterFunction(torch.autograd.Function):
         alpha = ops.launch_router_forward(z, router, router_activation)
         ctx.save_for_backward(z, router, alpha)
         ctx.router_activation = router_activation
+        ctx.set_materialize_grads(False)
         return alpha
 
     @staticmethod
     @once_differentiable
-    def backward(ctx, dalpha: torch.Tensor):
+    def backward(ctx, dalpha: torch.Tensor | None):
+        if dalpha is None:  # alpha reached the loss through no path: z and the router get no gradient
+            return None, None, None
         z, router, alpha = ctx.saved_tensors
         dz, drouter = ops.launch_router_backward(
             z, router, alpha, dalpha.contiguous(), ctx.router_activation,

@@ -20,6 +20,7 @@ import ctypes
 from typing import Sequence
 
 import torch
+from torch.autograd.function import once_differentiable
 
 from . import _lib
 from .api import MoC
@@ -137,17 +138,106 @@ def step_one(module: MoC, x: torch.Tensor, z: torch.Tensor, cache: torch.Tensor)
     return decode_step([module], [x], z, [cache])[0]
 
 
-def _proj_alpha(h: torch.Tensor, module: MoC, z: torch.Tensor | None, alpha: torch.Tensor | None) -> torch.Tensor:
+def _proj_alpha(h: torch.Tensor, module: MoC, z: torch.Tensor | None, alpha: torch.Tensor | None,
+                train: bool = False) -> torch.Tensor:
+    """The module's router output for the fused projection: ``alpha`` as given, or routed from z
+    (through the router's autograd function when ``train``, so dalpha reaches z and the router)."""
     B, T = h.shape[:2]
     from . import ops
+    from .api import _route
 
     if alpha is None:
         if z is None or z.shape[:2] != (B, T):
             raise ValueError(f"z must be [{B}, {T}, z_dim], got {None if z is None else tuple(z.shape)}")
-        alpha = ops.launch_router_forward(z.detach(), module.router.detach(), module.router_activation)
+        if train:
+            alpha = _route(z, module.router, module.router_activation)
+        else:
+            alpha = ops.launch_router_forward(z.detach(), module.router.detach(), module.router_activation)
     if alpha.shape != (B, T, module.k) or alpha.dtype != torch.bfloat16:
         raise ValueError(f"alpha must be bf16 [{B}, {T}, {module.k}], got {tuple(alpha.shape)} {alpha.dtype}")
-    return _aligned(alpha.detach())
+    return alpha if train else _aligned(alpha.detach())
+
+
+def _wants_grad(h, weight, modules, z, alphas) -> bool:
+    if not torch.is_grad_enabled():
+        return False
+    ts = [h, weight] + [p for m in modules for p in (m.conv_bases, m.router)]
+    ts += [z] if z is not None else list(alphas or ())
+    return any(t is not None and t.requires_grad for t in ts)
+
+
+class _ProjConvFunction(torch.autograd.Function):
+    """Training form of the fused projection + convolution, for one or more modules over one
+    projection weight (the reference's ``qkv_proj`` then ``q_conv`` / ``k_conv`` / ``v_conv``
+    under autograd, README.md:115-129).
+
+    Forward: one ``moc_proj_forward_multi_save`` launch gives each module's y and keeps its
+    rounded projection x (the tensor the unfused path's projection GEMM writes), so the
+    convolution reads no x back from memory.  Backward: each module's convolution backward on
+    its saved x (``moc_backward``: dx, dalpha, dbasis; reference moc/api.py:148-195), then the
+    projection's gradients as two library GEMMs over the modules' dx side by side:
+    dh = dx . weight and dweight = dx^T . h."""
+
+    @staticmethod
+    def forward(ctx, h, weight, spec, *alpha_basis):
+        # spec: per module (dim, activation flag); alpha_basis: alpha_0, basis_0, alpha_1, ...
+        B, T, Dm = h.shape
+        n = len(spec)
+        h2, w2 = _aligned(h), _aligned(weight)
+        alphas = [_aligned(a) for a in alpha_basis[0::2]]
+        bases = [_aligned(b) for b in alpha_basis[1::2]]
+        arr = (_lib.MocProjModule * n)()
+        x_ptrs = (ctypes.c_void_p * n)()
+        outs, xs = [], []
+        off = 0
+        for i, ((D, act), a, b) in enumerate(zip(spec, alphas, bases)):
+            out = torch.empty(B, T, D, dtype=torch.bfloat16, device=h.device)
+            x = torch.empty(B, T, D, dtype=torch.bfloat16, device=h.device)
+            outs.append(out)
+            xs.append(x)
+            x_ptrs[i] = x.data_ptr()
+            arr[i] = _lib.MocProjModule(dim=D, row_offset=off, n_bases=a.shape[-1], activation=act,
+                                        alpha=a.data_ptr(), basis=b.data_ptr(), out=out.data_ptr())
+            off += D
+        with torch.cuda.device(h.device):
+            rc = _lib.load().moc_proj_forward_multi_save(n, arr, x_ptrs, B, T, Dm, bases[0].shape[1], h2.data_ptr(),
+                                                         w2.data_ptr(), weight.shape[0], _lib.stream_of(h.device))
+        _lib.check(rc, "moc_proj_forward_multi_save")
+        ctx.save_for_backward(h2, w2, *xs, *alphas, *bases)
+        ctx.spec = spec
+        ctx.set_materialize_grads(False)  # an output outside the loss arrives as None: its module is skipped
+        return tuple(outs)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, *dys):
+        from . import ops
+
+        n = len(ctx.spec)
+        saved = ctx.saved_tensors
+        h2, w2 = saved[0], saved[1]
+        xs, alphas, bases = saved[2:2 + n], saved[2 + n:2 + 2 * n], saved[2 + 2 * n:]
+        B, T, Dm = h2.shape
+        N = B * T
+        need_proj = ctx.needs_input_grad[0] or ctx.needs_input_grad[1]
+        dxs, grads = [], []
+        for i, ((D, act), dy) in enumerate(zip(ctx.spec, dys)):
+            if dy is None:  # this module's output took no part in the loss
+                dxs.append(torch.zeros(B, T, D, dtype=torch.bfloat16, device=h2.device))
+                grads += [None, None]
+                continue
+            dx, dalpha, dbasis = ops.launch_backward(xs[i], alphas[i], bases[i], dy.contiguous(), dy,
+                                                     activation_flag=act, need_x=need_proj)
+            dxs.append(dx)
+            grads += [dalpha, dbasis]
+        dh = dw = None
+        if need_proj:
+            dx_all = (dxs[0] if n == 1 else torch.cat(dxs, dim=-1)).view(N, -1)
+            if ctx.needs_input_grad[0]:
+                dh = torch.mm(dx_all, w2).view(B, T, Dm)
+            if ctx.needs_input_grad[1]:
+                dw = torch.mm(dx_all.t(), h2.view(N, Dm))
+        return (dh, dw, None, *grads)
 
 
 def proj_forward_multi(h: torch.Tensor, weight: torch.Tensor, modules: Sequence[MoC], z: torch.Tensor | None = None,
@@ -164,7 +254,10 @@ def proj_forward_multi(h: torch.Tensor, weight: torch.Tensor, modules: Sequence[
     z:       the routing input for every module, or ``alphas``: each module's router output.
 
     h is read once for all modules; each module's projection is rounded to bf16 and
-    convolved on chip.  Forward only (no autograd graph).  Returns the modules' outputs."""
+    convolved on chip.  Returns the modules' outputs.  When autograd records (grad enabled and
+    h, weight, z / alphas or a module's parameters require grad) the launch also keeps each
+    module's projection for the backward, and the outputs carry the graph: gradients reach h,
+    weight, z (through the routers) and every module's conv_bases and router."""
     if not 1 <= len(modules) <= _lib.PROJ_MAX_MODULES:
         raise ValueError(f"proj_forward_multi takes 1 to {_lib.PROJ_MAX_MODULES} modules, got {len(modules)}")
     if h.ndim != 3 or h.dtype != torch.bfloat16 or not h.is_cuda:
@@ -181,6 +274,12 @@ def proj_forward_multi(h: torch.Tensor, weight: torch.Tensor, modules: Sequence[
         raise ValueError("pass exactly one of z (routing input) or alphas (router outputs)")
     if alphas is not None and len(alphas) != len(modules):
         raise ValueError("one alpha per module")
+    if _wants_grad(h, weight, modules, z, alphas):
+        ab = []
+        for i, m in enumerate(modules):
+            ab += [_proj_alpha(h, m, z, None if alphas is None else alphas[i], train=True), m.conv_bases]
+        spec = tuple((m.dim, int(m.activation is not None)) for m in modules)
+        return list(_ProjConvFunction.apply(h, weight, spec, *ab))
     h2, w2 = _aligned(h.detach()), _aligned(weight.detach())
     keep, outs = [h2, w2], []
     arr = (_lib.MocProjModule * len(modules))()
@@ -211,9 +310,10 @@ def proj_forward(h: torch.Tensor, weight: torch.Tensor, module: MoC, z: torch.Te
             for the reference's attention block, the q, k or v rows of qkv_proj.weight).
     z:      the routing input [B, T, z_dim]; or ``alpha`` [B, T, module.k], the router output.
 
-    Forward only (no autograd graph): inference and prefill.  The projection is rounded to
-    bf16 before the convolution, as a bf16 qkv tensor is; the result matches the unfused
-    path up to the order of the projection's fp32 sums."""
+    The projection is rounded to bf16 before the convolution, as a bf16 qkv tensor is; the
+    result matches the unfused path up to the order of the projection's fp32 sums.  Under
+    autograd (grad enabled and an input or the module's parameters require grad) the launch
+    also keeps the projection for the backward, as ``proj_forward_multi`` does."""
     if h.ndim != 3 or h.dtype != torch.bfloat16 or not h.is_cuda:
         raise ValueError(f"h must be a CUDA bf16 tensor [B, T, in_dim], got {tuple(h.shape)} {h.dtype}")
     B, T, Dm = h.shape
@@ -223,6 +323,10 @@ def proj_forward(h: torch.Tensor, weight: torch.Tensor, module: MoC, z: torch.Te
         raise ValueError("proj_forward needs a bf16 module")
     if (alpha is None) == (z is None):
         raise ValueError("pass exactly one of z (routing input) or alpha (router output)")
+    if _wants_grad(h, weight, [module], z, None if alpha is None else [alpha]):
+        a2 = _proj_alpha(h, module, z, alpha, train=True)
+        spec = ((module.dim, int(module.activation is not None)),)
+        return _ProjConvFunction.apply(h, weight, spec, a2, module.conv_bases)[0]
     a2 = _proj_alpha(h, module, z, alpha)
     h2, w2 = _aligned(h.detach()), _aligned(weight.detach())
     basis = _aligned(module.conv_bases.detach())
