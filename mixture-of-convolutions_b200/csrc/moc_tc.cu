@@ -146,7 +146,9 @@ struct Layout {
   // per-warp output staging: one 16-row x 16-channel bf16 block (32-byte rows)
   static constexpr int ost_bytes = BWD ? 0 : 8 * 16 * 32;
   // (the SiLU backward needs no staging of its own: it writes dz, bf16, over dy in the tile)
-  static constexpr int total = 1024 + 2 * stage_bytes + head_bytes + ost_bytes + 64;
+  // SiLU backward: the dz rows an item hands to the item before it (up to 7 rows x 128 channels)
+  static constexpr int carry_bytes = (BWD && ACT) ? 8 * kBD * 2 : 0;
+  static constexpr int total = 1024 + 2 * stage_bytes + head_bytes + carry_bytes + ost_bytes + 64;
   static constexpr int min_blocks = BWD ? ((BREG && KT == 1) ? 2 : 1) : ((KT == 1 && S <= 4) ? 4 : 2);
 };
 
@@ -194,6 +196,7 @@ struct Smem {
   uint32_t stages;  // 2 stages, 1024-byte aligned
   char* stages_p;
   char* head;       // basis staging / dalpha reduction
+  char* carry;      // SiLU backward: dz rows handed from one item to the next
   char* ost;        // per-warp output staging
   uint32_t bar;     // 2 mbarriers
   __device__ explicit Smem(char* raw) {
@@ -201,7 +204,8 @@ struct Smem {
     stages_p = base;
     stages = smem_addr(base);
     head = base + 2 * L::stage_bytes;
-    ost = head + L::head_bytes;
+    carry = head + L::head_bytes;
+    ost = carry + L::carry_bytes;
     bar = smem_addr(ost + L::ost_bytes);
   }
 };
@@ -493,6 +497,12 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
   const int64_t i1 = i0 + a.items_per_group < n_items ? i0 + a.items_per_group : n_items;
   const bool want_dx = DXDA && a.dx != nullptr;
   const int ch_w = warp * 16;  // this warp's channel offset inside the slice
+  // With SiLU the CTA runs its items last to first.  The dx taps of an item read dz up to S - 1
+  // rows past its end, which are the first rows of the next item: computed there already (its
+  // pre-activation, from the same x, alpha and basis, in the same order), they are handed over
+  // through `sm.carry` instead of being recomputed as a fifth 16-row block.
+  auto item_of = [&](int64_t it) { return ACT ? i0 + i1 - 1 - it : it; };
+  int64_t prev_ss = -1, prev_r0 = -1;  // sequence start and first row of the item run before
 
   // per-lane constants: basis rows (padded, unswizzled), alpha rows (dense), and the
   // swizzled x / dy boxes holding this warp's 16 channels (chunks 2*(warp&3)+{0,1})
@@ -553,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
     }
     if (threadIdx.x == 0) {
       int64_t ss, se, r0, r1;
-      if (a.rm.item(i0, ss, se, r0, r1))
+      if (a.rm.item(item_of(i0), ss, se, r0, r1))
         issue_tile<L, true>(&xmap, &dymap, &amap, sm.stages, sm.bar, r0, ch_base);
       else
         mbar_arrive(sm.bar);
@@ -588,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       int64_t ss, se, r0, r1;
       const uint32_t nbar = sm.bar + 8 * (cur ^ 1);
       if constexpr (DXDA) bulk_wait_read<0>();
-      if (a.rm.item(it + 1, ss, se, r0, r1))
+      if (a.rm.item(item_of(it + 1), ss, se, r0, r1))
         issue_tile<L, true>(&xmap, &dymap, &amap, sm.stages + (cur ^ 1) * L::stage_bytes, nbar, r0, ch_base);
       else
         mbar_arrive(nbar);
@@ -608,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       }
     }
     int64_t ss, se, r0, r1;
-    const bool valid = a.rm.item(it, ss, se, r0, r1);
+    const bool valid = a.rm.item(item_of(it), ss, se, r0, r1);
     char* stage_p = sm.stages_p + cur * L::stage_bytes;
     const uint32_t x_s = sm.stages + cur * L::stage_bytes;
     const uint32_t a_s = x_s + L::x_bytes + L::dy_bytes;
@@ -671,7 +681,11 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       // rounded to bf16 and written over dy in the stage (each lane its own pairs), so phase 2
       // is the plain backward on dz
       if constexpr (ACT) {
-        for (int b = 0; b < 5; ++b) {
+        // the next item (run just before this one) continues this item's sequence: its first
+        // S - 1 dz rows are this item's rows kTile.., kept in sm.carry
+        const bool carried = prev_ss == ss && prev_r0 == r1 && r1 < se && r1 - r0 == kTile;  // uniform
+        const int nb1 = carried ? 4 : 5;
+        for (int b = 0; b < nb1; ++b) {
           float pre[2][4] = {};
           if (16 * b < se - r0) {
 #pragma unroll
@@ -691,17 +705,32 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
               }
             }
           }
+          // dy of the block in the fragment order of pre (register 2 nt + h: rows g + 8 h,
+          // channels 8 nt + 2 q, + 1), times silu'(pre), back over dy
+          uint32_t d[4];
+          ldsm_x4(dy_addr(16 * b), d);
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int row = 16 * b + g + 8 * h;
-              const int chunk = 2 * (warp & 3) + nt;  // 16-byte chunk of (row, ch_w + 8nt)
-              uint32_t* d = reinterpret_cast<uint32_t*>(stage_p + dy_box + row * 128 + (((chunk ^ row) & 7) << 4) + 4 * q);
               const float2 ds = dsilu_bf2(pre[nt][2 * h], pre[nt][2 * h + 1]);
-              const float2 o = __fmul2_rn(make_float2(bf_lo(*d), bf_hi(*d)), ds);
-              *d = pack_bf16(o.x, o.y);
+              const float2 o = __fmul2_rn(make_float2(bf_lo(d[2 * nt + h]), bf_hi(d[2 * nt + h])), ds);
+              d[2 * nt + h] = pack_bf16(o.x, o.y);
             }
+          stsm_x4(dy_addr(16 * b), d[0], d[1], d[2], d[3]);
+        }
+        __syncwarp();
+        // the warp's 16 channels of rows 0 .. S - 2 (two 16-byte chunks a row): lane 2 r + hf
+        // takes the carried rows into rows kTile + r, then leaves its own rows r for the item
+        // that runs next (the same words of sm.carry, read before they are written)
+        if (lane < 2 * (S - 1)) {
+          const int r = lane >> 1, chunk = 2 * (warp & 3) + (lane & 1);
+          uint4* cw = reinterpret_cast<uint4*>(sm.carry + r * (kBD * 2) + (ch_w + 8 * (lane & 1)) * 2);
+          if (carried) {
+            const int row = kTile + r;
+            *reinterpret_cast<uint4*>(stage_p + dy_box + row * 128 + (((chunk ^ row) & 7) << 4)) = *cw;
+          }
+          *cw = *reinterpret_cast<const uint4*>(stage_p + dy_box + r * 128 + (((chunk ^ r) & 7) << 4));
         }
         __syncwarp();
       }
@@ -841,6 +870,10 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
     } else {
 #pragma unroll 1
       for (int b = 0; b < nb; ++b) block(b);
+    }
+    if constexpr (ACT) {
+      prev_ss = valid ? ss : -1;
+      prev_r0 = valid ? r0 : -1;
     }
     // the next iteration's wait barrier orders these reads of red_s and the stage before reuse
   }
