@@ -35,6 +35,24 @@ def test_proj_forward_multi_checks_modules_and_weight_before_launch():
         fused.proj_forward_multi(h, torch.randn(96, 32).bfloat16(), mods, z=h)
 
 
+def test_proj_training_launch_only_when_autograd_records():
+    """The fused projection keeps each module's projection for a backward only when a gradient can
+    flow: grad mode on, and h, the weight, the routing input (or the router outputs) or a module's
+    parameters requiring grad.  Otherwise it is the inference launch."""
+    m = _mod()
+    h = torch.randn(1, 8, 32).bfloat16()
+    w = torch.randn(64, 32).bfloat16()
+    assert fused._wants_grad(h, w, [m], h, None)  # conv_bases and router are parameters
+    with torch.no_grad():
+        assert not fused._wants_grad(h, w, [m], h, None)
+    m.requires_grad_(False)
+    assert not fused._wants_grad(h, w, [m], h, None)
+    assert not fused._wants_grad(h, w, [m], None, [torch.zeros(1, 8, 16)])
+    assert fused._wants_grad(h, w, [m], None, [torch.zeros(1, 8, 16, requires_grad=True)])
+    assert fused._wants_grad(h.clone().requires_grad_(), w, [m], h, None)
+    assert fused._wants_grad(h, w.clone().requires_grad_(), [m], h, None)
+
+
 def test_decode_step_shape_checks():
     m = _mod()
     x = torch.randn(2, 1, 64).bfloat16()
