@@ -22,7 +22,9 @@ init_std 0.002, router weight N(0, 0.02); x, z, dy ~ N(0, 1) from a seeded gener
                  config-2 batch, rank 0 at N=1 only.
 * ``workloads``  (default workload, N=1) short runs of the other BASELINE workloads on
                  the same GPU: config 3 (varlen), config 4 (decode) and config 5 (large,
-                 one GPU's share), each with its own value and roofline.
+                 one GPU's share), each with its own value and roofline; and the fused
+                 q / k / v projection + convolution (proj): prefill, and its training step
+                 fused against unfused.
 
 With N > 1 (torchrun, one rank per GPU) every rank runs its own config-2 batch
 (weak scaling) and the step adds one all-reduce of [dconv_bases | drouter]; after the
