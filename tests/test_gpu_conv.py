@@ -189,6 +189,34 @@ def test_varlen_ragged_lengths_and_boundaries(kernel_path, xdt):
     _assert_close(got, ref, xdt, "ragged")
 
 
+@pytest.mark.parametrize("K,S,path", [(16, 4, 0), (32, 8, 2)], ids=["k16s4", "k32s8_warp_bwd"])
+@pytest.mark.parametrize("lengths", [None, [1024, 960, 64, 1000, 1048], [70, 2000, 2026]],
+                         ids=["fixed", "aligned", "ragged"])
+def test_silu_backward_hands_dz_rows_between_items(lengths, K, S, path):
+    """With SiLU a CTA of the warp-level backward runs its 64-token items last to first, and each
+    item hands its first S - 1 dz rows to the item before it.  At D = 2048 a CTA takes several
+    items (16 channel slices share the SMs), so hand-overs happen inside sequences. They must not
+    happen across sequence boundaries, whether those fall on item boundaries (fixed: 1088 = 17
+    items, so one CTA holds the last item of sequence 0 and the first of sequence 1; aligned:
+    1024, 1984, 2048, ...) or inside items (ragged).  32 bases with 8 taps take the two-pass
+    warp-level kernel here (moc_set_kernel_path(MOC_PATH_WARP_BACKWARD)); both passes hand over."""
+    D = 2048
+    _lib.set_kernel_path(path)
+    try:
+        if lengths is None:
+            x, a, dy, basis = _inputs(2, 1088, D, K, S, seed=41)
+            got, ref = _run(x, a, basis, dy, torch.bfloat16, torch.bfloat16, torch.bfloat16, "silu")
+        else:
+            cu = torch.tensor([0] + torch.tensor(lengths).cumsum(0).tolist(), dtype=torch.int32)
+            x, a, dy, basis = _inputs(1, int(cu[-1]), D, K, S, seed=42)
+            got, ref = _run(x[0], a[0], basis, dy[0], torch.bfloat16, torch.bfloat16, torch.bfloat16, "silu",
+                            cu=cu, max_seqlen=max(lengths))
+    finally:
+        _lib.set_kernel_path(0)
+    _assert_close(got, ref, torch.bfloat16, "hand-over")
+    assert _lib.device_status(clear=True) == 0
+
+
 @pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float32], ids=["bf16", "fp32"])
 def test_varlen_boundaries_are_bit_exact(kernel_path, xdt):
     """Poisoning every other sequence (x, dy times 1000) leaves the outputs of one
