@@ -649,15 +649,21 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
       const int r = row0 + lrow;
       return x_s + dy_box + r * 128 + (((m_chunk ^ r) & 7) << 4);
     };
-    // W fragments (C layout) for alpha rows starting at tile row ar, tap s.
-    auto w_frag = [&](int ar, int s, float (&w)[2][4], uint32_t lean_off) {
+    // alpha fragments (the A operand of W) of tile rows ar .. ar + 15
+    auto alpha_frag = [&](int ar, uint32_t (&af)[KT][4], uint32_t lean_off) {
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt) {
-        uint32_t af[4];
         if constexpr (kLean)  // KT == 1: lean_off is the lane's offset of rows (ar & 15) + lrow
-          ldsm_x4(a_s + (ar & ~15) * L::ARB + lean_off, af);
+          ldsm_x4(a_s + (ar & ~15) * L::ARB + lean_off, af[kt]);
         else
-          ldsm_x4(a_s + (ar & ~15) * L::ARB + alpha_off<L>((ar & 15) + lrow, 2 * kt + (lane >> 4)), af);
+          ldsm_x4(a_s + (ar & ~15) * L::ARB + alpha_off<L>((ar & 15) + lrow, 2 * kt + (lane >> 4)), af[kt]);
+      }
+    };
+    // W fragments (C layout) of tap s from alpha fragments
+    auto w_of = [&](const uint32_t (&afs)[KT][4], int s, float (&w)[2][4]) {
+#pragma unroll
+      for (int kt = 0; kt < KT; ++kt) {
+        const uint32_t(&af)[4] = afs[kt];
         uint32_t b0, b1, b2, b3;
         if constexpr (BREG) {
           b0 = bw[s][kt][0], b1 = bw[s][kt][1], b2 = bw[s][kt][2], b3 = bw[s][kt][3];
@@ -675,6 +681,12 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
         }
       }
     };
+    // W fragments for alpha rows starting at tile row ar, tap s
+    auto w_frag = [&](int ar, int s, float (&w)[2][4], uint32_t lean_off) {
+      uint32_t af[KT][4];
+      alpha_frag(ar, af, lean_off);
+      w_of(af, s, w);
+    };
 
     if (valid) {
       // ---- phase 1 (SiLU): dz = dy * silu'(pre) for tile rows 0..79 (future rows feed dx),
@@ -688,11 +700,13 @@ __global__ void __launch_bounds__(kThreads, (Layout<KT, S, ACT, true, PART>::min
         for (int b = 0; b < nb1; ++b) {
           float pre[2][4] = {};
           if (16 * b < se - r0) {
+            uint32_t af[KT][4];  // the block's own alpha rows serve every tap
+            alpha_frag(16 * b, af, a0o);
 #pragma unroll
             for (int s = 0; s < S; ++s) {
               const int j = S - 1 - s;
               float w[2][4];
-              w_frag(16 * b, s, w, a0o);
+              w_of(af, s, w);
               uint32_t xr[4];
               if constexpr (kLean)
                 ldsm_x4(x_s + xo[s] + b * 2048, xr);
